@@ -1,0 +1,139 @@
+/*
+ * rans_b200.h -- C ABI of the B200 (sm_100a) entropy-coded weight GEMV library
+ * (librans_b200.so).  Plain pointers, sizes and an int status; no C++ or
+ * framework types cross this boundary.
+ *
+ * Bitstream ("tile-interleaved rANS", unchanged from the reference
+ * snuri00/vram-compression, kernel/rans_gemv.cu:1-15 and kernel/rans.py:55-98):
+ *   - W (rows x cols) holds integer codes; W_real[r,c] = code[r,c] * step[c].
+ *   - The matrix is cut into tiles of R rows x C columns; tile t = rb*ncb + cb
+ *     (ncb = cols / C).  Lane l (0..31) of a tile owns columns l, l+32, ... and
+ *     stores them as one rANS stream s = t*32 + l in the order
+ *       for k in 0..C/32-1: for r in 0..R-1: code[rb*R + r][cb*C + l + 32k].
+ *   - 32-bit state in [2^16, 2^32), 16-bit renormalisation words, 12-bit
+ *     probabilities, one static table per matrix:
+ *       table[slot] = sym | freq << 8 | (slot - cum[sym]) << 20,  sym = code + 128.
+ *   - words: uint16, each stream = [state >> 16, state & 0xffff, payload...],
+ *     followed by 8 zero pad words after the last stream; offs: uint32 word
+ *     offset of every stream (rows*cols*32/(R*C) entries).
+ *
+ * All launchers are asynchronous on `stream`, allocate nothing unless stated,
+ * and return 0 on success, a CUDA error code (as int) after a failed launch,
+ * -1 for an unsupported R, or -2 for a shape the tiling cannot describe
+ * (rows % R, cols % C or C % 32 non-zero).
+ */
+#ifndef RANS_B200_H
+#define RANS_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#ifndef __CUDA_RUNTIME_H__
+typedef struct CUstream_st* cudaStream_t;
+#endif
+
+#define RANS_B200_ABI_VERSION 1
+
+/* ---------------------------------------------------------------- drop-in
+ * The three entry points of the reference library, same names, argument
+ * meaning and error convention, so a ctypes/cffi/cgo binding written for the
+ * reference's librans.so loads this library unchanged.                    */
+
+/* y[rows] (fp32) = code . x  where x (fp32[cols]) is already multiplied by
+ * the per-column step.  When cols != C the caller zero-fills y first (the
+ * reference accumulates column blocks with atomic adds); when cols == C y is
+ * overwritten.  R in {1,2,4,8,16}.
+ * Replaces kernel/rans_gemv.cu:146-153 (launch_rans_gemv). */
+int launch_rans_gemv(int R, const void* words, const void* offs, const void* table,
+                     const void* x, void* y, int rows, int cols, int C,
+                     cudaStream_t stream);
+
+/* out (bf16, rows x cols row-major) = bf16(code * step[col]).
+ * Replaces kernel/rans_gemv.cu:155-162 (launch_rans_decode). */
+int launch_rans_decode(int R, const void* words, const void* offs, const void* table,
+                       const void* step, void* out, int rows, int cols, int C,
+                       cudaStream_t stream);
+
+/* Fixed-rate 4-bit baseline: w = uint32[rows][cols/8], nibble b of word j
+ * holds code+8 of column 8j+b; y[rows] = sum (q-8) * x[col]; cols % 32 == 0.
+ * Replaces kernel/rans_gemv.cu:164-170 (launch_int4_gemv). */
+int launch_int4_gemv(const void* w, const void* x, void* y, int rows, int cols,
+                     cudaStream_t stream);
+
+/* ---------------------------------------------------------------- additive */
+
+/* Same GEMV with the step folded inside the kernel: x is bf16[cols], step is
+ * fp32[cols]; y (fp32[rows]) is overwritten (no zero-fill needed).
+ * nwords = total length of `words` in words (including the 8 pad words), or
+ * -1 when unknown (the stream holding the matrix's last words is then read
+ * straight from global memory instead of being staged).
+ * Additive variant of kernel/rans.py:140-152 (RansMatrix.gemv), whose host
+ * multiply x.float()*step (rans.py:141) moves into the kernel. */
+int rans_gemv_bf16(int R, const void* words, const void* offs, const void* table,
+                   const void* x_bf16, const void* step, void* y, int rows, int cols,
+                   int C, int64_t nwords, cudaStream_t stream);
+
+/* One encoded matrix (one linear projection) for the step launcher.
+ * Device pointers.  x is bf16[cols] when step != NULL, else fp32[cols]
+ * already multiplied by the step.  y (fp32[rows]) is overwritten. */
+typedef struct RansGemvDesc {
+    const void* words;   /* uint16 stream words                     */
+    const void* offs;    /* uint32 word offset per stream           */
+    const void* table;   /* uint32[4096] slot table (layout above)  */
+    const void* x;       /* activation                              */
+    const void* step;    /* fp32 per-column step or NULL            */
+    void* y;             /* fp32 output                             */
+    int64_t nwords;      /* words length incl. pad, or -1 if unknown */
+    int32_t rows, cols, C;
+    int32_t reserved;    /* must be 0                               */
+} RansGemvDesc;
+
+/* Bytes of device workspace the step launcher needs for these n descriptors
+ * (all tiled with the same R); negative on a bad R (-1) or shape (-2). */
+int64_t rans_gemv_step_workspace_bytes(const RansGemvDesc* descs, int n, int R);
+
+/* Encode the work plan of n matrices (HOST array `descs`) into the caller's
+ * device `workspace` and return the launch grid in *grid_out.  Call once, and
+ * again whenever a descriptor changes; it synchronises `stream`.  Returns -3
+ * when workspace_bytes is too small. */
+int rans_gemv_step_plan(const RansGemvDesc* descs, int n, int R, void* workspace,
+                        size_t workspace_bytes, int* grid_out, cudaStream_t stream);
+
+/* Run every projection of a decoder step from ONE grid (one kernel launch,
+ * capturable in a CUDA graph).  Each CTA loads the slot table of its matrix
+ * and its warps decode whole row blocks, so y is stored without atomics.
+ * No counterpart in the reference: its harness launches one kernel per
+ * matrix (kernel/bench.py:104-107, kernel/rans.py:147-151). */
+int rans_gemv_step_launch(int R, const void* workspace, int grid, cudaStream_t stream);
+
+/* ------------------------------------------------------------ host encoder
+ * Bit-exact C++ restatement of the reference producer kernel/rans.py:34-98
+ * (build_table, lane_order, encode), multithreaded over tiles.            */
+
+/* table[4096] and freq/cum[256] (int32) from int8 codes.  Returns 0, or 1
+ * for a single-symbol distribution (kernel/rans.py:45). */
+int rans_build_table_host(const int8_t* codes, int64_t n, uint32_t* table,
+                          int32_t* freq, int32_t* cum, int nthreads);
+
+/* Upper bound of the words array length for a shape (streams*(n+2)+8). */
+int64_t rans_encode_bound(int rows, int cols, int R, int C);
+
+/* Encode int8 codes (row-major rows x cols) with `table`.  Writes offs
+ * (one per stream), words (*nwords_out including the 8 pad words, at most
+ * words_cap) and per-stream lengths are implied by offs.  Returns 0, -2 for
+ * a bad shape, -3 when words_cap is too small. */
+int rans_encode_host(const int8_t* codes, int rows, int cols, int R, int C,
+                     const uint32_t* table, uint16_t* words, int64_t words_cap,
+                     uint32_t* offs, int64_t* nwords_out, int nthreads);
+
+/* ABI version (RANS_B200_ABI_VERSION). */
+int rans_b200_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* RANS_B200_H */

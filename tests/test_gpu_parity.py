@@ -1,0 +1,183 @@
+"""GPU parity: librans_b200 against the oracle (and the reference's own outputs
+recorded in tests/golden), through the C ABI.
+
+Bars (from the reference's kernel/bench.py:38-66 and the task's north star):
+  * decoded codes bit-exact (decode with step = 1 returns bf16(code) exactly);
+  * decode to bf16 equals bf16(code * step) bit for bit (bench.py:49-51);
+  * GEMV: relative L2 <= 1e-3 against float64 dequantise-then-matvec, and the
+    reference's own max-abs-relative bound 1e-4 (bench.py:52-56);
+  * int4 baseline: allclose(rtol=1e-4, atol=1e-3) (bench.py:65).
+"""
+import ctypes
+import os
+
+import numpy as np
+import pytest
+
+from conftest import GOLDEN, ROOT, golden_cases, load_case
+from oracle import rans_oracle as orc
+
+pytestmark = pytest.mark.gpu
+
+CASES = golden_cases()
+IDS = [os.path.basename(p)[:-4] for p in CASES]
+REL_L2 = 1e-3      # north-star GEMV tolerance
+MAX_REL = 1e-4     # kernel/bench.py:55
+
+
+@pytest.fixture(scope="module")
+def torch(cuda_ok):
+    import torch as t
+    return t
+
+
+@pytest.fixture(scope="module")
+def rb():
+    import rans_b200
+    rans_b200.load()
+    return rans_b200
+
+
+def _y64(codes, step, x):
+    return orc.gemv(codes, step.astype(np.float64), x.astype(np.float64))
+
+
+def _check_y(y, yref):
+    y = np.asarray(y, np.float64)
+    assert orc.rel_l2(y, yref) <= REL_L2
+    assert np.abs(y - yref).max() / max(np.abs(yref).max(), 1e-30) < MAX_REL
+
+
+@pytest.mark.parametrize("path", CASES, ids=IDS)
+def test_decode_bit_exact(torch, rb, path):
+    codes, enc, step, x, y, _ = load_case(path)
+    m = rb.RansMatrix(enc, torch.ones(codes.shape[1]))
+    got = m.decode().float().cpu().numpy()
+    assert np.array_equal(got.astype(np.int64), codes)
+    m2 = rb.RansMatrix(enc, torch.from_numpy(step))
+    dec = m2.decode().cpu()
+    want = (torch.from_numpy(codes).float() * torch.from_numpy(step)).bfloat16()
+    assert torch.equal(dec, want)
+
+
+@pytest.mark.parametrize("path", CASES, ids=IDS)
+def test_gemv_dropin(torch, rb, path):
+    codes, enc, step, x, y, _ = load_case(path)
+    m = rb.RansMatrix(enc, torch.from_numpy(step))
+    got = m.gemv(torch.from_numpy(x).cuda()).cpu().numpy()
+    _check_y(got, y)
+    # an explicit, dirty y buffer is zeroed by the wrapper when cols != C
+    yb = torch.full((m.rows,), 7.0, device="cuda")
+    got2 = m.gemv(torch.from_numpy(x).cuda(), yb).cpu().numpy()
+    _check_y(got2, y)
+
+
+@pytest.mark.parametrize("path", CASES, ids=IDS)
+def test_gemv_bf16_fused_step(torch, rb, path):
+    codes, enc, step, x, y, _ = load_case(path)
+    m = rb.RansMatrix(enc, torch.from_numpy(step))
+    xb = torch.from_numpy(x).bfloat16()
+    yref = _y64(codes, step, xb.float().numpy())
+    got = m.gemv_bf16(xb.cuda(), torch.full((m.rows,), float("nan"), device="cuda")).cpu().numpy()
+    _check_y(got, yref)
+
+
+def test_step_launcher_matches_single(torch, rb):
+    mats, xs, ys, refs = [], [], [], []
+    for path in CASES:
+        codes, enc, step, x, y, _ = load_case(path)
+        if enc["R"] != 8:
+            continue
+        m = rb.RansMatrix(enc, torch.from_numpy(step))
+        xb = torch.from_numpy(x).bfloat16().cuda()
+        mats.append(m)
+        xs.append(xb)
+        ys.append(torch.full((m.rows,), float("nan"), device="cuda"))
+        refs.append(_y64(codes, step, xb.float().cpu().numpy()))
+    assert len(mats) >= 3
+    step = rb.RansStep(mats, xs, ys)
+    for _ in range(2):
+        step()
+        torch.cuda.synchronize()
+        for yv, yr in zip(ys, refs):
+            _check_y(yv.cpu().numpy(), yr)
+
+
+@pytest.mark.parametrize("shape,R,C,dist,bits", [
+    ((1536, 1536), 8, 512, "laplace", 3.25),
+    ((8960, 1536), 8, 512, "gauss", 4.25),       # config 2 gate/up
+    ((1536, 8960), 8, 640, "gauss", 4.25),       # config 2 down
+    ((512, 2048), 16, 512, "laplace", 2.25),     # config 3, R=16
+    ((256, 1024), 4, 1024, "laplace", 2.25),     # row mode, R=4
+])
+def test_large_against_c_oracle(torch, rb, shape, R, C, dist, bits):
+    rows, cols = shape
+    codes = orc.synth_codes(rows, cols, bits, dist, seed=rows + cols)
+    rng = np.random.default_rng(rows)
+    step = (0.01 * rng.uniform(0.5, 1.5, cols)).astype(np.float32)
+    x = rng.standard_normal(cols).astype(np.float32)
+    enc = rb.encode(codes, R, C)
+    m = rb.RansMatrix(enc, torch.from_numpy(step))
+    xb = torch.from_numpy(x).bfloat16()
+    xs = xb.float().numpy().astype(np.float64) * step.astype(np.float64)
+    yref = orc.c_decode_gemv(enc, xs, threads=8)
+    _check_y(m.gemv_bf16(xb.cuda()).cpu().numpy(), yref)
+    yref32 = orc.c_decode_gemv(enc, x.astype(np.float64) * step.astype(np.float32).astype(np.float64), threads=8)
+    _check_y(m.gemv(torch.from_numpy(x).cuda()).cpu().numpy(), yref32)
+    dec = m.decode().cpu()
+    want = (torch.from_numpy(codes).float() * torch.from_numpy(step)).bfloat16()
+    assert torch.equal(dec, want)
+
+
+def test_unstaged_fallback_high_entropy(torch, rb):
+    """Spans larger than the shared-memory stage (8 bits/symbol, R=16, C=1024)
+    take the global-memory path; results must not change."""
+    rng = np.random.default_rng(3)
+    codes = rng.integers(-128, 128, (64, 2048)).astype(np.int32)
+    step = rng.uniform(0.5, 1.5, 2048).astype(np.float32)
+    x = rng.standard_normal(2048).astype(np.float32)
+    enc = rb.encode(codes, 16, 1024)
+    m = rb.RansMatrix(enc, torch.from_numpy(step))
+    _check_y(m.gemv(torch.from_numpy(x).cuda()).cpu().numpy(), _y64(codes, step, x))
+    xb = torch.from_numpy(x).bfloat16()
+    _check_y(m.gemv_bf16(xb.cuda()).cpu().numpy(), _y64(codes, step, xb.float().numpy()))
+    dec = m.decode().float().cpu().numpy()
+    assert np.array_equal(dec, (torch.from_numpy(codes).float() * torch.from_numpy(step)).bfloat16().float().numpy())
+
+
+def test_int4_baseline(torch, rb):
+    """kernel/bench.py:59-66: int4 codes, default_rng(1), 256x1024."""
+    codes = np.random.default_rng(1).integers(-8, 8, size=(256, 1024))
+    g = torch.Generator().manual_seed(0)
+    step = torch.rand(1024, generator=g) + 0.5
+    m4 = rb.Int4Matrix(codes, step)
+    x = torch.randn(1024, generator=g).cuda()
+    y_ref = torch.from_numpy(codes).float().cuda() @ (x * step.cuda())
+    assert torch.allclose(m4.gemv(x), y_ref, rtol=1e-4, atol=1e-3)
+    for rows, cols in ((1536, 8960), (100, 64)):
+        c = np.random.default_rng(rows).integers(-8, 8, size=(rows, cols))
+        s = torch.rand(cols, generator=g) + 0.5
+        xx = torch.randn(cols, generator=g).cuda()
+        mm = rb.Int4Matrix(c, s)
+        yr = torch.from_numpy(c).float().cuda() @ (xx * s.cuda())
+        assert torch.allclose(mm.gemv(xx), yr, rtol=1e-4, atol=1e-3)
+
+
+def test_reference_kernel_agrees(torch, rb):
+    """The reference's own kernel, compiled unmodified for sm_100a into
+    oracle/_ref, gives the same decode and (within fp32 order) the same GEMV."""
+    ref_so = os.path.join(ROOT, "oracle", "_ref", "librans_ref.so")
+    if not os.path.exists(ref_so):
+        pytest.skip("oracle/_ref/librans_ref.so not built")
+    ref = ctypes.CDLL(ref_so)
+    for f in (ref.launch_rans_gemv, ref.launch_rans_decode):
+        f.argtypes = [ctypes.c_int] + [ctypes.c_void_p] * 5 + [ctypes.c_int] * 3 + [ctypes.c_void_p]
+        f.restype = ctypes.c_int
+    codes, enc, step, x, y, _ = load_case(os.path.join(GOLDEN, "edge_gauss425_256x1536_R8_C512.npz"))
+    mine = rb.RansMatrix(enc, torch.from_numpy(step))
+    theirs = rb.RansMatrix(enc, torch.from_numpy(step), lib=ref)
+    assert torch.equal(mine.decode(), theirs.decode())
+    xt = torch.from_numpy(x).cuda()
+    a = mine.gemv(xt).cpu().numpy()
+    b = theirs.gemv(xt).cpu().numpy()
+    assert orc.rel_l2(a, b) < 1e-5

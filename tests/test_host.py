@@ -1,0 +1,117 @@
+"""Host-side product code on CPU: the C++ encoder against the reference's own
+outputs, and the C-ABI library's exported symbols against include/*.h."""
+import ctypes
+import glob
+import json
+import os
+import re
+import hashlib
+
+import numpy as np
+import pytest
+
+from conftest import GOLDEN, ROOT, golden_cases, load_case
+import rans_b200 as rb
+from oracle import rans_oracle as orc
+
+CASES = golden_cases()
+IDS = [os.path.basename(p)[:-4] for p in CASES]
+
+
+@pytest.fixture(scope="module")
+def lib():
+    return rb.build()
+
+
+def header_symbols():
+    names = set()
+    for h in glob.glob(os.path.join(ROOT, "include", "*.h")):
+        src = open(h).read()
+        src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+        for m in re.finditer(r"^\s*(?:int|int64_t|size_t|void)\s+\**\s*(\w+)\s*\(", src, flags=re.M):
+            names.add(m.group(1))
+    return sorted(names)
+
+
+def test_header_declares_reference_entry_points():
+    syms = header_symbols()
+    for name in ("launch_rans_gemv", "launch_rans_decode", "launch_int4_gemv"):
+        assert name in syms
+
+
+def test_library_exports_every_header_symbol(lib):
+    handle = ctypes.CDLL(rb.LIB)
+    missing = [s for s in header_symbols() if not hasattr(handle, s)]
+    assert not missing, f"not exported: {missing}"
+    assert lib.rans_b200_abi_version() == rb.ABI_VERSION
+
+
+def test_reference_argtypes_bind(lib):
+    # the reference's build() binds exactly these; they must be present and callable types
+    for f in (lib.launch_rans_gemv, lib.launch_rans_decode):
+        assert len(f.argtypes) == 10
+    assert len(lib.launch_int4_gemv.argtypes) == 6
+
+
+@pytest.mark.parametrize("path", CASES, ids=IDS)
+def test_cpp_encoder_bit_exact(lib, path):
+    codes, enc, *_, bits = load_case(path)
+    for nt in (1, 3):
+        mine = rb.encode(codes, enc["R"], enc["C"], nthreads=nt)
+        assert np.array_equal(mine["table"], enc["table"])
+        assert np.array_equal(mine["offs"], enc["offs"])
+        assert np.array_equal(mine["words"], enc["words"])
+    np.testing.assert_allclose([mine["bits_payload"], mine["bits_state_offs"], mine["bits_table"],
+                                mine["entropy_model"]], bits, rtol=1e-12, atol=1e-9)
+
+
+def test_cpp_encoder_config1(lib):
+    meta = json.load(open(os.path.join(GOLDEN, "config1.json")))
+    codes = orc.synth_codes(meta["rows"], meta["cols"], meta["target_bits"], meta["dist"], meta["seed"])
+    enc = rb.encode(codes, meta["R"], meta["C"])
+    sha = lambda a: hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()
+    assert sha(enc["words"]) == meta["sha_words"]
+    assert sha(enc["offs"]) == meta["sha_offs"]
+    assert sha(enc["table"]) == meta["sha_table"]
+
+
+@pytest.mark.parametrize("path", CASES, ids=IDS)
+def test_cpp_table(lib, path):
+    codes, enc, *_ = load_case(path)
+    f, c, t = rb.build_table(orc.codes_to_symbols(codes))
+    f2, c2, t2 = orc.build_table(orc.codes_to_symbols(codes))
+    assert np.array_equal(t, enc["table"]) and np.array_equal(f, f2) and np.array_equal(c, c2)
+
+
+def test_encoder_random_shapes_against_oracle(lib):
+    rng = np.random.default_rng(5)
+    for trial in range(6):
+        R = int(rng.choice([1, 2, 4, 8, 16]))
+        C = int(32 * rng.integers(1, 6))
+        rows, cols = R * int(rng.integers(1, 5)), C * int(rng.integers(1, 4))
+        codes = np.clip(np.round(rng.laplace(0, rng.uniform(0.3, 8), (rows, cols))), -128, 127).astype(np.int32)
+        codes.flat[0] = 1  # never single-symbol
+        codes.flat[-1] = -1
+        a = rb.encode(codes, R, C, nthreads=2)
+        b = orc.encode(codes, R, C)
+        for k in ("words", "offs", "table"):
+            assert np.array_equal(a[k], b[k]), (trial, k)
+
+
+def test_encoder_errors(lib):
+    with pytest.raises(AssertionError):
+        rb.encode(np.zeros((8, 64), np.int32), 8, 64)          # single symbol
+    with pytest.raises(ValueError):
+        rb.encode(np.full((8, 64), 300), 8, 64)                # out of alphabet
+    with pytest.raises(AssertionError):
+        rb.encode(np.ones((8, 64)), 3, 64)                     # rows % R
+    assert lib.rans_encode_bound(8, 60, 8, 60) == -2
+
+
+def test_launchers_reject_bad_arguments_without_launching(lib):
+    # argument checks happen before any CUDA call, so these run without a GPU
+    assert lib.launch_rans_gemv(3, None, None, None, None, None, 6, 64, 64, None) == -1
+    assert lib.launch_rans_gemv(8, None, None, None, None, None, 12, 64, 64, None) == -2
+    assert lib.launch_rans_decode(8, None, None, None, None, None, 16, 64, 48, None) == -2
+    assert lib.launch_int4_gemv(None, None, None, 4, 40, None) == -2
+    assert lib.rans_gemv_bf16(5, None, None, None, None, None, None, 8, 64, 64, -1, None) == -1

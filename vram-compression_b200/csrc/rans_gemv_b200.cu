@@ -1,0 +1,701 @@
+// Fused rANS-decode + batch-1 GEMV for B200 (sm_100a).
+//
+// Bitstream: the reference's tile-interleaved rANS (kernel/rans_gemv.cu:1-15,
+// kernel/rans.py:55-98); see include/rans_b200.h for the format.
+//
+// Execution model (differs from the reference's one-stream-per-lane, one
+// global load per renormalisation, kernel/rans_gemv.cu:39-77):
+//   * a warp owns a WORK ITEM: in column mode (ncb > 1) a row block rb and a
+//     range of its column blocks, in row mode (ncb == 1) up to KROW row blocks.
+//     The item's tiles are consecutive in stream order, so their word streams
+//     form ONE contiguous span of `words`.
+//   * the span is staged into a per-warp shared-memory buffer with 16-byte
+//     cp.async copies (fully coalesced), and every renormalisation word is then
+//     read from shared memory instead of global memory;
+//   * each lane decodes K independent streams (lane l of K tiles) interleaved
+//     symbol by symbol, hiding the table-lookup -> multiply -> compare chain;
+//   * the 16 KB slot table is re-laid in shared memory as
+//       sym | bias << 8 | freq << 20
+//     so freq is one shift, and the code value is built with one byte-permute
+//     as the float 2^23 + sym, minus 2^23 + 128;
+//   * fp32 accumulation; the R (or K*R) partial sums per lane are combined with
+//     a transpose-reduce (reduce-scatter) butterfly, R-1 + log2(32/R) shuffles
+//     instead of 5*R, and stored without atomics whenever a warp covers every
+//     column block of its rows.
+#include <cstdint>
+#include <cstdlib>
+#include <cstring>
+#include <vector>
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include "../../include/rans_b200.h"
+
+namespace rb200 {
+
+constexpr int kScaleBits = 12;
+constexpr uint32_t kProbM = 1u << kScaleBits;
+constexpr uint32_t kRansL = 1u << 16;
+constexpr int kPadWords = 8;
+constexpr int kWarps = 8;                 // warps per CTA
+constexpr int kThreads = kWarps * 32;
+constexpr int kStageBytes = 8192;         // per-warp staging buffer
+constexpr int kTableBytes = kProbM * 4;
+constexpr int kSmemBytes = kTableBytes + kWarps * kStageBytes;
+
+// Device view of one matrix plus its work decomposition.
+struct MatDev {
+    const uint16_t* words;
+    const uint32_t* offs;
+    const uint32_t* table;
+    const void* x;
+    const float* step;     // NULL: x is fp32 pre-scaled; else x is bf16
+    float* y;
+    int64_t nwords;        // incl. pad, or -1
+    int rows, cols, C, ncb, nrb, nk;
+    int rowmode;           // 1: ncb == 1, item = KROW row blocks
+    int kcol;              // column-mode streams per lane (2..4)
+    int nseg, cbs;         // column-mode segments per row block, cbs per segment
+    int nitems;
+    int accumulate;        // 1: atomicAdd into y (split rows), 0: store
+    int pad_[3];
+};
+
+struct Chunk {             // one CTA of the step launcher
+    int desc, item0, nitems, pad_;
+};
+
+struct StepHeader {
+    int ndesc, nchunks, R, pad_;
+};
+
+// ------------------------------------------------------------ primitives
+__device__ __forceinline__ void cp_async16(uint32_t saddr, const void* gptr) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(saddr), "l"(gptr));
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;\n" ::: "memory"); }
+
+// Reference table entry sym | freq<<8 | bias<<20  ->  sym | bias<<8 | freq<<20.
+__device__ __forceinline__ uint32_t relayout_entry(uint32_t e) {
+    return (e & 0xFFu) | ((e >> 20) << 8) | (((e >> 8) & 0xFFFu) << 20);
+}
+
+__device__ __forceinline__ void load_table(uint32_t* tab, const uint32_t* __restrict__ table) {
+    for (int i = threadIdx.x; i < (int)kProbM; i += blockDim.x) tab[i] = relayout_entry(__ldg(table + i));
+}
+
+// Signed code of a re-laid entry as an exact float: bits 0x4B0000ss = 2^23 + sym.
+__device__ __forceinline__ float entry_code(uint32_t e) {
+    return __int_as_float(__byte_perm(e, 0x4B000000u, 0x7540)) - 8388736.0f;
+}
+
+template <bool BF16X>
+__device__ __forceinline__ float load_x(const MatDev& d, int c) {
+    if (BF16X) {
+        const __nv_bfloat16* xb = reinterpret_cast<const __nv_bfloat16*>(d.x);
+        return __bfloat162float(xb[c]) * __ldg(d.step + c);
+    } else {
+        return __ldg(reinterpret_cast<const float*>(d.x) + c);
+    }
+}
+
+// Transpose-reduce V values (power of two <= 32) across the warp.  Lane l ends
+// with the full 32-lane sum of value index l >> (5 - log2 V).
+template <int V>
+__device__ __forceinline__ float reduce_scatter(float (&v)[V], int lane) {
+    int m = 16;
+#pragma unroll
+    for (int h = V / 2; h >= 1; h >>= 1) {
+        const bool up = (lane & m) != 0;
+#pragma unroll
+        for (int i = 0; i < h; ++i) {
+            const float send = up ? v[i] : v[i + h];
+            const float keep = up ? v[i + h] : v[i];
+            v[i] = keep + __shfl_xor_sync(0xffffffffu, send, m);
+        }
+        m >>= 1;
+    }
+    float s = v[0];
+    for (; m >= 1; m >>= 1) s += __shfl_xor_sync(0xffffffffu, s, m);
+    return s;
+}
+
+template <int V>
+struct Log2 { static constexpr int value = 1 + Log2<V / 2>::value; };
+template <>
+struct Log2<1> { static constexpr int value = 0; };
+
+// ------------------------------------------------------------ staging
+// Span of words [w0, w1) (word indices into d.words).  Copies the 16-byte
+// aligned chunks covering it into `stage` and returns the stage index of word
+// w0.  Every copied chunk contains at least one byte of the span, so no chunk
+// touches a page the span does not touch.
+__device__ __forceinline__ uint32_t stage_span(const MatDev& d, uint16_t* stage, uint32_t w0,
+                                               uint64_t w1, int lane) {
+    const uintptr_t b0 = reinterpret_cast<uintptr_t>(d.words) + 2ull * w0;
+    const uintptr_t b1 = reinterpret_cast<uintptr_t>(d.words) + 2ull * w1;
+    const uintptr_t a0 = b0 & ~uintptr_t(15);
+    const uintptr_t a1 = (b1 + 15) & ~uintptr_t(15);
+    const uint32_t s = static_cast<uint32_t>(__cvta_generic_to_shared(stage));
+    const int n16 = static_cast<int>((a1 - a0) >> 4);
+    for (int i = lane; i < n16; i += 32) cp_async16(s + 16u * i, reinterpret_cast<const void*>(a0 + 16ull * i));
+    cp_async_commit();
+    cp_async_wait_all();
+    __syncwarp();
+    return static_cast<uint32_t>((b0 - a0) >> 1);
+}
+
+// Bytes a staged span [w0, w1) occupies (+16 for the one-word look-ahead).
+__device__ __forceinline__ uint64_t staged_bytes(const MatDev& d, uint32_t w0, uint64_t w1) {
+    const uintptr_t b0 = reinterpret_cast<uintptr_t>(d.words) + 2ull * w0;
+    const uintptr_t b1 = reinterpret_cast<uintptr_t>(d.words) + 2ull * w1;
+    return ((b1 + 15) & ~uintptr_t(15)) - (b0 & ~uintptr_t(15)) + 16;
+}
+
+// End (exclusive word index) of the span that ends at stream `s_end`
+// (one past the last stream of the span), or UINT64_MAX when unknown.
+__device__ __forceinline__ uint64_t span_end(const MatDev& d, int64_t s_end) {
+    const int64_t nstreams = (int64_t)d.nrb * d.ncb * 32;
+    if (s_end < nstreams) return d.offs[s_end];
+    if (d.nwords >= 0) return (uint64_t)(d.nwords - kPadWords);
+    return UINT64_MAX;
+}
+
+// ------------------------------------------------------------ decode core
+// Decodes one pass: K streams per lane, C/32 k-steps of R symbols each.
+// wb/pos: word base (shared stage or global words) and per-stream word index
+// of the stream's first (state) word.  NACC == 1: all streams share rows
+// (column mode, acc[0][r]); NACC == K: stream j owns acc[j] (row mode, shared x).
+template <int R, int K, int NACC, bool BF16X>
+__device__ __forceinline__ void decode_pass(const uint32_t* __restrict__ tab, const uint16_t* wb,
+                                            const uint32_t (&pos)[K], const int (&xcol)[K], int kk,
+                                            const MatDev& d, float (&acc)[NACC][R], int& bad) {
+    uint32_t st[K], w[K], p[K];
+#pragma unroll
+    for (int j = 0; j < K; ++j) {
+        p[j] = pos[j];
+        st[j] = (static_cast<uint32_t>(wb[p[j]]) << 16) | wb[p[j] + 1];
+        p[j] += 2;
+        w[j] = wb[p[j]];
+    }
+    const int nk = d.nk;
+    for (int k = 0; k < nk; ++k) {
+        float xv[K];
+        if (NACC == K) {
+            const float v = load_x<BF16X>(d, xcol[0] + 32 * k);
+#pragma unroll
+            for (int j = 0; j < K; ++j) xv[j] = v;
+        } else {
+#pragma unroll
+            for (int j = 0; j < K; ++j) xv[j] = (j < kk) ? load_x<BF16X>(d, xcol[j] + 32 * k) : 0.f;
+        }
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+#pragma unroll
+            for (int j = 0; j < K; ++j) {
+                const uint32_t e = tab[st[j] & (kProbM - 1)];
+                st[j] = (e >> 20) * (st[j] >> kScaleBits) + ((e >> 8) & 0xFFFu);
+                if (st[j] < kRansL) {
+                    st[j] = __byte_perm(w[j], st[j], 0x5410);
+                    ++p[j];
+                    w[j] = wb[p[j]];
+                }
+                float& a = acc[NACC == 1 ? 0 : j][r];
+                a = fmaf(entry_code(e), xv[j], a);
+            }
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < K; ++j)
+        if (j < kk && st[j] != kRansL) ++bad;
+}
+
+// Sets up a pass over tiles [t0, t0+kk) (consecutive), staging when possible,
+// and decodes it.  Streams j >= kk replay stream kk-1 with zero activation.
+template <int R, int K, int NACC, bool BF16X>
+__device__ __forceinline__ void run_pass(const MatDev& d, const uint32_t* tab, uint16_t* stage,
+                                         int64_t t0, int kk, const int (&xcol)[K],
+                                         float (&acc)[NACC][R], int& bad, int lane) {
+    const int64_t s0 = t0 * 32;
+    const uint32_t w0 = d.offs[s0];
+    const uint64_t w1 = span_end(d, s0 + 32ll * kk);
+    uint32_t pos[K];
+#pragma unroll
+    for (int j = 0; j < K; ++j) pos[j] = d.offs[s0 + 32 * (j < kk ? j : kk - 1) + lane];
+    if (w1 != UINT64_MAX && staged_bytes(d, w0, w1) <= (uint64_t)kStageBytes) {
+        const uint32_t head = stage_span(d, stage, w0, w1, lane);
+#pragma unroll
+        for (int j = 0; j < K; ++j) pos[j] = pos[j] - w0 + head;
+        decode_pass<R, K, NACC, BF16X>(tab, stage, pos, xcol, kk, d, acc, bad);
+        __syncwarp();   // stage is rewritten by the next pass
+    } else {
+        decode_pass<R, K, NACC, BF16X>(tab, d.words, pos, xcol, kk, d, acc, bad);
+    }
+}
+
+// Column mode: rows rb*R..rb*R+R-1, column blocks of segment `seg`.
+template <int R, int K, bool BF16X>
+__device__ void colmode_item(const MatDev& d, int item, const uint32_t* tab, uint16_t* stage,
+                             int lane, int& bad) {
+    const int rb = item / d.nseg;
+    const int seg = item - rb * d.nseg;
+    const int cb_begin = seg * d.cbs;
+    const int cb_end = min(d.ncb, cb_begin + d.cbs);
+    float acc[1][R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) acc[0][r] = 0.f;
+    for (int cb0 = cb_begin; cb0 < cb_end; cb0 += K) {
+        const int kk = min(K, cb_end - cb0);
+        int xcol[K];
+#pragma unroll
+        for (int j = 0; j < K; ++j) xcol[j] = (cb0 + (j < kk ? j : 0)) * d.C + lane;
+        run_pass<R, K, 1, BF16X>(d, tab, stage, (int64_t)rb * d.ncb + cb0, kk, xcol, acc, bad, lane);
+    }
+    const float s = reduce_scatter<R>(acc[0], lane);
+    constexpr int kShift = 5 - Log2<R>::value;
+    if ((lane & ((1 << kShift) - 1)) == 0) {
+        const int row = rb * R + (lane >> kShift);
+        if (d.accumulate) atomicAdd(d.y + row, s);
+        else d.y[row] = s;
+    }
+}
+
+// Row mode (ncb == 1): KR consecutive row blocks, one stream each per lane.
+template <int R, int KR, bool BF16X>
+__device__ void rowmode_item(const MatDev& d, int item, const uint32_t* tab, uint16_t* stage,
+                             int lane, int& bad) {
+    const int rb0 = item * KR;
+    const int kk = min(KR, d.nrb - rb0);
+    float acc[KR][R];
+#pragma unroll
+    for (int j = 0; j < KR; ++j)
+#pragma unroll
+        for (int r = 0; r < R; ++r) acc[j][r] = 0.f;
+    int xcol[KR];
+#pragma unroll
+    for (int j = 0; j < KR; ++j) xcol[j] = lane;
+    run_pass<R, KR, KR, BF16X>(d, tab, stage, rb0, kk, xcol, acc, bad, lane);
+    float* flat = &acc[0][0];
+    float v[KR * R];
+#pragma unroll
+    for (int i = 0; i < KR * R; ++i) v[i] = flat[i];
+    const float s = reduce_scatter<KR * R>(v, lane);
+    constexpr int kShift = 5 - Log2<KR * R>::value;
+    const int idx = lane >> kShift;          // = j*R + r
+    if ((lane & ((1 << kShift) - 1)) == 0 && idx / R < kk) d.y[(rb0 + idx / R) * R + idx % R] = s;
+}
+
+template <int R>
+struct RowK { static constexpr int value = (R >= 8) ? 32 / R : 4; };
+
+template <int R, bool BF16X>
+__device__ __forceinline__ void process_item(const MatDev& d, int item, const uint32_t* tab,
+                                             uint16_t* stage, int lane, int& bad) {
+    if (d.rowmode) {
+        rowmode_item<R, RowK<R>::value, BF16X>(d, item, tab, stage, lane, bad);
+    } else {
+        switch (d.kcol) {
+            case 2: colmode_item<R, 2, BF16X>(d, item, tab, stage, lane, bad); break;
+            case 3: colmode_item<R, 3, BF16X>(d, item, tab, stage, lane, bad); break;
+            default: colmode_item<R, 4, BF16X>(d, item, tab, stage, lane, bad); break;
+        }
+    }
+}
+
+// ------------------------------------------------------------ kernels
+// One matrix: CTA b handles items [b*kWarps, b*kWarps + kWarps).
+template <int R, bool BF16X>
+__global__ void __launch_bounds__(kThreads) gemv_matrix_kernel(MatDev d) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    uint32_t* tab = reinterpret_cast<uint32_t*>(smem);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    uint16_t* stage = reinterpret_cast<uint16_t*>(smem + kTableBytes + warp * kStageBytes);
+    load_table(tab, d.table);
+    __syncthreads();
+    const int item = blockIdx.x * kWarps + warp;
+    if (item >= d.nitems) return;
+    int bad = 0;
+    process_item<R, BF16X>(d, item, tab, stage, lane, bad);
+}
+
+// Every projection of a decoder step: CTA b processes chunk b (one matrix).
+template <int R>
+__global__ void __launch_bounds__(kThreads) gemv_step_kernel(const StepHeader* __restrict__ hdr) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    const MatDev* descs = reinterpret_cast<const MatDev*>(hdr + 1);
+    const Chunk* chunks = reinterpret_cast<const Chunk*>(descs + hdr->ndesc);
+    const Chunk ch = chunks[blockIdx.x];
+    const MatDev& d = descs[ch.desc];
+    uint32_t* tab = reinterpret_cast<uint32_t*>(smem);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    uint16_t* stage = reinterpret_cast<uint16_t*>(smem + kTableBytes + warp * kStageBytes);
+    load_table(tab, d.table);
+    __syncthreads();
+    if (warp >= ch.nitems) return;
+    int bad = 0;
+    const MatDev dl = d;
+    if (dl.step != nullptr) process_item<R, true>(dl, ch.item0 + warp, tab, stage, lane, bad);
+    else process_item<R, false>(dl, ch.item0 + warp, tab, stage, lane, bad);
+}
+
+// Decode-only: K consecutive tiles per warp, bf16(code * step) to a dense
+// row-major matrix (the "decompress, then cuBLAS" comparator).
+template <int R, int K>
+__global__ void __launch_bounds__(kThreads) decode_kernel(MatDev d, __nv_bfloat16* __restrict__ out,
+                                                          int64_t ntiles) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    uint32_t* tab = reinterpret_cast<uint32_t*>(smem);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    uint16_t* stage = reinterpret_cast<uint16_t*>(smem + kTableBytes + warp * kStageBytes);
+    load_table(tab, d.table);
+    __syncthreads();
+    const int64_t t0 = ((int64_t)blockIdx.x * kWarps + warp) * K;
+    if (t0 >= ntiles) return;
+    const int kk = ntiles - t0 < K ? (int)(ntiles - t0) : K;
+    const int64_t s0 = t0 * 32;
+    const uint32_t w0 = d.offs[s0];
+    const uint64_t w1 = span_end(d, s0 + 32ll * kk);
+    uint32_t pos[K];
+#pragma unroll
+    for (int j = 0; j < K; ++j) pos[j] = d.offs[s0 + 32 * (j < kk ? j : kk - 1) + lane];
+    const uint16_t* wb = d.words;
+    bool staged = false;
+    if (w1 != UINT64_MAX && staged_bytes(d, w0, w1) <= (uint64_t)kStageBytes) {
+        const uint32_t head = stage_span(d, stage, w0, w1, lane);
+#pragma unroll
+        for (int j = 0; j < K; ++j) pos[j] = pos[j] - w0 + head;
+        staged = true;
+    }
+    uint32_t st[K], w[K], p[K];
+    int64_t obase[K];
+    int cbase[K];
+#pragma unroll
+    for (int j = 0; j < K; ++j) {
+        const int64_t t = t0 + (j < kk ? j : kk - 1);
+        const int rb = (int)(t / d.ncb), cb = (int)(t % d.ncb);
+        obase[j] = (int64_t)rb * R * d.cols;
+        cbase[j] = cb * d.C + lane;
+    }
+    auto body = [&](const uint16_t* base) {
+#pragma unroll
+        for (int j = 0; j < K; ++j) {
+            p[j] = pos[j];
+            st[j] = (static_cast<uint32_t>(base[p[j]]) << 16) | base[p[j] + 1];
+            p[j] += 2;
+            w[j] = base[p[j]];
+        }
+        for (int k = 0; k < d.nk; ++k) {
+            float sv[K];
+#pragma unroll
+            for (int j = 0; j < K; ++j) sv[j] = __ldg(d.step + cbase[j] + 32 * k);
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+#pragma unroll
+                for (int j = 0; j < K; ++j) {
+                    const uint32_t e = tab[st[j] & (kProbM - 1)];
+                    st[j] = (e >> 20) * (st[j] >> kScaleBits) + ((e >> 8) & 0xFFFu);
+                    if (st[j] < kRansL) {
+                        st[j] = __byte_perm(w[j], st[j], 0x5410);
+                        ++p[j];
+                        w[j] = base[p[j]];
+                    }
+                    if (j < kk)
+                        out[obase[j] + (int64_t)r * d.cols + cbase[j] + 32 * k] =
+                            __float2bfloat16(entry_code(e) * sv[j]);
+                }
+            }
+        }
+    };
+    if (staged) body(stage);
+    else body(wb);
+}
+
+// Fixed-rate int4 baseline: one warp per row, 16-byte (32-code) loads.
+__global__ void __launch_bounds__(256) int4_gemv_kernel(const uint4* __restrict__ w,
+                                                        const float4* __restrict__ x,
+                                                        float* __restrict__ y, int rows, int cols) {
+    const int lane = threadIdx.x & 31;
+    const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    if (row >= rows) return;
+    const int nchunk = cols / 32;
+    const uint4* wr = w + (int64_t)row * nchunk;
+    float acc = 0.f;
+#pragma unroll 2
+    for (int j = lane; j < nchunk; j += 32) {
+        const uint4 q = __ldg(wr + j);
+        const uint32_t qs[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+        for (int a = 0; a < 4; ++a) {
+            const float4 x0 = __ldg(x + j * 8 + a * 2);
+            const float4 x1 = __ldg(x + j * 8 + a * 2 + 1);
+            const float xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+#pragma unroll
+            for (int b = 0; b < 8; ++b)
+                acc = fmaf((float)((int)((qs[a] >> (4 * b)) & 15u) - 8), xv[b], acc);
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (lane == 0) y[row] = acc;
+}
+
+// ------------------------------------------------------------ host side
+static bool valid_R(int R) { return R == 1 || R == 2 || R == 4 || R == 8 || R == 16; }
+
+static int row_k(int R) { return R >= 8 ? 32 / R : 4; }
+
+static int sm_count() {
+    int dev = 0, n = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    return n;
+}
+
+// Fills the work decomposition of d.  `split_for` > 0 asks for at least that
+// many items (column blocks then split across warps, accumulating into y).
+static void plan_matrix(MatDev& d, int R, int split_for) {
+    d.ncb = d.cols / d.C;
+    d.nrb = d.rows / R;
+    d.nk = d.C / 32;
+    d.rowmode = d.ncb == 1 ? 1 : 0;
+    d.accumulate = 0;
+    if (d.rowmode) {
+        const int kr = row_k(R);
+        d.kcol = 0;
+        d.nseg = 1;
+        d.cbs = 1;
+        d.nitems = (d.nrb + kr - 1) / kr;
+        return;
+    }
+    // K that divides ncb (no idle stream slots), preferring more streams per lane
+    int k = 4;
+    if (d.ncb % 4 == 0) k = 4;
+    else if (d.ncb % 3 == 0) k = 3;
+    else if (d.ncb % 2 == 0) k = 2;
+    else k = d.ncb < 4 ? d.ncb : 3;
+    if (k < 2) k = 2;
+    d.kcol = k;
+    const int passes = (d.ncb + k - 1) / k;
+    int nseg = 1;
+    if (split_for > 0) {
+        while (nseg < passes && (int64_t)d.nrb * nseg < split_for) ++nseg;
+        while (passes % nseg) ++nseg;   // equal segments
+    }
+    d.nseg = nseg;
+    d.cbs = (passes / nseg) * k;
+    d.nitems = d.nrb * nseg;
+    d.accumulate = nseg > 1 ? 1 : 0;
+}
+
+// The dynamic shared-memory opt-in is per function and per device; remember
+// which (function, device) pairs are done.
+static bool set_smem_attr(const void* fn, unsigned long long* done_mask) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return false;
+    const unsigned long long bit = 1ull << (dev & 63);
+    if (__atomic_load_n(done_mask, __ATOMIC_ACQUIRE) & bit) return true;
+    if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes) != cudaSuccess)
+        return false;
+    __atomic_fetch_or(done_mask, bit, __ATOMIC_ACQ_REL);
+    return true;
+}
+
+template <int R>
+static int launch_matrix(const MatDev& d, bool bf16x, cudaStream_t stream) {
+    const int grid = (d.nitems + kWarps - 1) / kWarps;
+    if (grid == 0) return 0;
+    if (bf16x) {
+        static unsigned long long done = 0;
+        set_smem_attr((const void*)gemv_matrix_kernel<R, true>, &done);
+        gemv_matrix_kernel<R, true><<<grid, kThreads, kSmemBytes, stream>>>(d);
+    } else {
+        static unsigned long long done = 0;
+        set_smem_attr((const void*)gemv_matrix_kernel<R, false>, &done);
+        gemv_matrix_kernel<R, false><<<grid, kThreads, kSmemBytes, stream>>>(d);
+    }
+    return (int)cudaGetLastError();
+}
+
+static int dispatch_matrix(int R, const MatDev& d, bool bf16x, cudaStream_t stream) {
+    switch (R) {
+        case 1: return launch_matrix<1>(d, bf16x, stream);
+        case 2: return launch_matrix<2>(d, bf16x, stream);
+        case 4: return launch_matrix<4>(d, bf16x, stream);
+        case 8: return launch_matrix<8>(d, bf16x, stream);
+        case 16: return launch_matrix<16>(d, bf16x, stream);
+        default: return -1;
+    }
+}
+
+static bool shape_ok(int R, int rows, int cols, int C) {
+    return rows > 0 && cols > 0 && C > 0 && C % 32 == 0 && cols % C == 0 && rows % R == 0;
+}
+
+static MatDev make_desc(const void* words, const void* offs, const void* table, const void* x,
+                        const void* step, void* y, int rows, int cols, int C, int64_t nwords) {
+    MatDev d;
+    std::memset(&d, 0, sizeof(d));
+    d.words = static_cast<const uint16_t*>(words);
+    d.offs = static_cast<const uint32_t*>(offs);
+    d.table = static_cast<const uint32_t*>(table);
+    d.x = x;
+    d.step = static_cast<const float*>(step);
+    d.y = static_cast<float*>(y);
+    d.nwords = nwords;
+    d.rows = rows;
+    d.cols = cols;
+    d.C = C;
+    return d;
+}
+
+// Enough warps to occupy the GPU for single-matrix launches.
+static int split_target() { return sm_count() * 16; }
+
+}  // namespace rb200
+
+using namespace rb200;
+
+extern "C" int launch_rans_gemv(int R, const void* words, const void* offs, const void* table,
+                                const void* x, void* y, int rows, int cols, int C,
+                                cudaStream_t stream) {
+    if (!valid_R(R)) return -1;
+    if (!shape_ok(R, rows, cols, C)) return -2;
+    MatDev d = make_desc(words, offs, table, x, nullptr, y, rows, cols, C, -1);
+    // the caller zero-fills y when cols != C (reference contract), so column
+    // blocks may be split across warps and accumulated
+    plan_matrix(d, R, cols != C ? split_target() : 0);
+    return dispatch_matrix(R, d, false, stream);
+}
+
+extern "C" int rans_gemv_bf16(int R, const void* words, const void* offs, const void* table,
+                              const void* x_bf16, const void* step, void* y, int rows, int cols,
+                              int C, int64_t nwords, cudaStream_t stream) {
+    if (!valid_R(R)) return -1;
+    if (!shape_ok(R, rows, cols, C) || step == nullptr) return -2;
+    MatDev d = make_desc(words, offs, table, x_bf16, step, y, rows, cols, C, nwords);
+    plan_matrix(d, R, 0);   // y is overwritten: whole row blocks per warp
+    return dispatch_matrix(R, d, true, stream);
+}
+
+template <int R, int K>
+static int launch_decode_t(const MatDev& d, void* out, cudaStream_t stream) {
+    const int64_t ntiles = (int64_t)d.nrb * d.ncb;
+    const int64_t warps = (ntiles + K - 1) / K;
+    const int grid = (int)((warps + kWarps - 1) / kWarps);
+    static unsigned long long done = 0;
+    set_smem_attr((const void*)decode_kernel<R, K>, &done);
+    decode_kernel<R, K><<<grid, kThreads, kSmemBytes, stream>>>(d, static_cast<__nv_bfloat16*>(out), ntiles);
+    return (int)cudaGetLastError();
+}
+
+extern "C" int launch_rans_decode(int R, const void* words, const void* offs, const void* table,
+                                  const void* step, void* out, int rows, int cols, int C,
+                                  cudaStream_t stream) {
+    if (!valid_R(R)) return -1;
+    if (!shape_ok(R, rows, cols, C)) return -2;
+    MatDev d = make_desc(words, offs, table, nullptr, step, nullptr, rows, cols, C, -1);
+    d.ncb = cols / C;
+    d.nrb = rows / R;
+    d.nk = C / 32;
+    switch (R) {
+        case 1: return launch_decode_t<1, 2>(d, out, stream);
+        case 2: return launch_decode_t<2, 2>(d, out, stream);
+        case 4: return launch_decode_t<4, 2>(d, out, stream);
+        case 8: return launch_decode_t<8, 2>(d, out, stream);
+        case 16: return launch_decode_t<16, 2>(d, out, stream);
+        default: return -1;
+    }
+}
+
+extern "C" int launch_int4_gemv(const void* w, const void* x, void* y, int rows, int cols,
+                                cudaStream_t stream) {
+    if (rows <= 0 || cols <= 0 || cols % 32) return -2;
+    const int threads = 256;
+    const int grid = (int)(((int64_t)rows * 32 + threads - 1) / threads);
+    int4_gemv_kernel<<<grid, threads, 0, stream>>>(static_cast<const uint4*>(w), static_cast<const float4*>(x),
+                                                   static_cast<float*>(y), rows, cols);
+    return (int)cudaGetLastError();
+}
+
+// ------------------------------------------------------------ step launcher
+static size_t step_bytes(int ndesc, int64_t nchunks) {
+    return sizeof(StepHeader) + sizeof(MatDev) * (size_t)ndesc + sizeof(Chunk) * (size_t)nchunks;
+}
+
+static int64_t count_chunks(const RansGemvDesc* descs, int n, int R, std::vector<MatDev>* out) {
+    int64_t nchunks = 0;
+    for (int i = 0; i < n; ++i) {
+        const RansGemvDesc& s = descs[i];
+        if (!shape_ok(R, s.rows, s.cols, s.C)) return -1;
+        MatDev d = make_desc(s.words, s.offs, s.table, s.x, s.step, s.y, s.rows, s.cols, s.C, s.nwords);
+        plan_matrix(d, R, 0);
+        nchunks += (d.nitems + kWarps - 1) / kWarps;
+        if (out) out->push_back(d);
+    }
+    return nchunks;
+}
+
+extern "C" int64_t rans_gemv_step_workspace_bytes(const RansGemvDesc* descs, int n, int R) {
+    if (!valid_R(R) || n <= 0) return -1;
+    const int64_t nchunks = count_chunks(descs, n, R, nullptr);
+    if (nchunks < 0) return -2;
+    return (int64_t)step_bytes(n, nchunks);
+}
+
+extern "C" int rans_gemv_step_plan(const RansGemvDesc* descs, int n, int R, void* workspace,
+                                   size_t workspace_bytes, int* grid_out, cudaStream_t stream) {
+    if (!valid_R(R)) return -1;
+    if (n <= 0) return -2;
+    std::vector<MatDev> mats;
+    const int64_t nchunks = count_chunks(descs, n, R, &mats);
+    if (nchunks < 0) return -2;
+    if (step_bytes(n, nchunks) > workspace_bytes) return -3;
+    std::vector<uint8_t> host(step_bytes(n, nchunks));
+    StepHeader* h = reinterpret_cast<StepHeader*>(host.data());
+    h->ndesc = n;
+    h->nchunks = (int)nchunks;
+    h->R = R;
+    MatDev* md = reinterpret_cast<MatDev*>(h + 1);
+    Chunk* ch = reinterpret_cast<Chunk*>(md + n);
+    int64_t c = 0;
+    for (int i = 0; i < n; ++i) {
+        md[i] = mats[i];
+        for (int it = 0; it < mats[i].nitems; it += kWarps) {
+            ch[c].desc = i;
+            ch[c].item0 = it;
+            ch[c].nitems = mats[i].nitems - it < kWarps ? mats[i].nitems - it : kWarps;
+            ch[c].pad_ = 0;
+            ++c;
+        }
+    }
+    if (grid_out) *grid_out = (int)nchunks;
+    cudaError_t e = cudaMemcpyAsync(workspace, host.data(), host.size(), cudaMemcpyHostToDevice, stream);
+    if (e != cudaSuccess) return (int)e;
+    // the pageable source must stay valid until the copy has been staged
+    e = cudaStreamSynchronize(stream);
+    return (int)e;
+}
+
+template <int R>
+static int launch_step_t(const void* ws, int nchunks, cudaStream_t stream) {
+    static unsigned long long done = 0;
+    set_smem_attr((const void*)gemv_step_kernel<R>, &done);
+    gemv_step_kernel<R><<<nchunks, kThreads, kSmemBytes, stream>>>(static_cast<const StepHeader*>(ws));
+    return (int)cudaGetLastError();
+}
+
+extern "C" int rans_gemv_step_launch(int R, const void* workspace, int grid, cudaStream_t stream) {
+    const int nchunks = grid;
+    if (nchunks <= 0) return 0;
+    switch (R) {
+        case 1: return launch_step_t<1>(workspace, nchunks, stream);
+        case 2: return launch_step_t<2>(workspace, nchunks, stream);
+        case 4: return launch_step_t<4>(workspace, nchunks, stream);
+        case 8: return launch_step_t<8>(workspace, nchunks, stream);
+        case 16: return launch_step_t<16>(workspace, nchunks, stream);
+        default: return -1;
+    }
+}
+
+extern "C" int rans_b200_abi_version(void) { return RANS_B200_ABI_VERSION; }
