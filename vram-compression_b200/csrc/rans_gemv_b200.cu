@@ -38,9 +38,15 @@ constexpr int kScaleBits = 12;
 constexpr uint32_t kProbM = 1u << kScaleBits;
 constexpr uint32_t kRansL = 1u << 16;
 constexpr int kPadWords = 8;
-constexpr int kWarps = 8;                 // warps per CTA
+#ifndef RB_WARPS
+#define RB_WARPS 8
+#endif
+#ifndef RB_STAGE_BYTES
+#define RB_STAGE_BYTES 8192
+#endif
+constexpr int kWarps = RB_WARPS;          // warps per CTA
 constexpr int kThreads = kWarps * 32;
-constexpr int kStageBytes = 8192;         // per-warp staging buffer
+constexpr int kStageBytes = RB_STAGE_BYTES;  // per-warp staging buffer (0: no staging)
 constexpr int kTableBytes = kProbM * 4;
 constexpr int kSmemBytes = kTableBytes + kWarps * kStageBytes;
 
@@ -224,7 +230,7 @@ __device__ __forceinline__ void run_pass(const MatDev& d, const uint32_t* tab, u
     uint32_t pos[K];
 #pragma unroll
     for (int j = 0; j < K; ++j) pos[j] = d.offs[s0 + 32 * (j < kk ? j : kk - 1) + lane];
-    if (w1 != UINT64_MAX && staged_bytes(d, w0, w1) <= (uint64_t)kStageBytes) {
+    if (kStageBytes > 0 && w1 != UINT64_MAX && staged_bytes(d, w0, w1) <= (uint64_t)kStageBytes) {
         const uint32_t head = stage_span(d, stage, w0, w1, lane);
 #pragma unroll
         for (int j = 0; j < K; ++j) pos[j] = pos[j] - w0 + head;
@@ -362,7 +368,7 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(MatDev d, __nv_bfloat1
     for (int j = 0; j < K; ++j) pos[j] = d.offs[s0 + 32 * (j < kk ? j : kk - 1) + lane];
     const uint16_t* wb = d.words;
     bool staged = false;
-    if (w1 != UINT64_MAX && staged_bytes(d, w0, w1) <= (uint64_t)kStageBytes) {
+    if (kStageBytes > 0 && w1 != UINT64_MAX && staged_bytes(d, w0, w1) <= (uint64_t)kStageBytes) {
         const uint32_t head = stage_span(d, stage, w0, w1, lane);
 #pragma unroll
         for (int j = 0; j < K; ++j) pos[j] = pos[j] - w0 + head;
