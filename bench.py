@@ -188,7 +188,7 @@ class ClockSampler:
 
     def __init__(self, gpu_index):
         self.gpu = gpu_index
-        self.rows = []
+        self.rows = []          # (arrival time, fields)
         self.proc = None
 
     def start(self):
@@ -203,28 +203,32 @@ class ClockSampler:
 
     def _read(self):
         for line in self.proc.stdout:
-            self.rows.append([v.strip() for v in line.split(",")])
+            self.rows.append((time.time(), [v.strip() for v in line.split(",")]))
 
-    def stop(self):
+    def stop(self, t0, t1):
+        """Summarise the samples that arrived inside the timed window [t0, t1]."""
         if self.proc is None:
             return None
+        time.sleep(0.15)
         self.proc.terminate()
         try:
             self.proc.wait(timeout=5)
         except Exception:
             self.proc.kill()
         self.th.join(timeout=2)
-        sm = [float(r[1]) for r in self.rows if len(r) > 8 and r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in self.rows if len(r) > 8 and r[2].replace(".", "").isdigit()]
+        rows = [r for t, r in self.rows if t0 <= t <= t1 + 0.1 and len(r) > 8]
+        isnum = lambda v: v.replace(".", "", 1).isdigit()
+        sm = [float(r[1]) for r in rows if isnum(r[1])]
+        mx = [float(r[2]) for r in rows if isnum(r[2])]
+        pw = [float(r[3]) for r in rows if isnum(r[3])]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = set()
-        for r in self.rows:
-            if len(r) > 8:
-                for i, n in enumerate(names):
-                    if r[5 + i].lower() == "active":
-                        reasons.add(n)
+        for r in rows:
+            for i, n in enumerate(names):
+                if r[5 + i].lower() == "active":
+                    reasons.add(n)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": sorted(reasons), "samples": len(sm)}
+                "power_w_max": max(pw) if pw else None, "reasons": sorted(reasons), "samples": len(sm)}
 
 
 # ----------------------------------------------------------------- CPU path
@@ -234,14 +238,14 @@ def cpu_decode_gemv_sample(mats_host, budget_s, threads):
     Returns (weights processed, seconds)."""
     from oracle import rans_oracle as orc
     done_w, spent = 0, 0.0
-    for enc, xs in mats_host:
-        t = time.perf_counter()
-        orc.c_decode_gemv(enc, xs, threads=threads)
-        spent += time.perf_counter() - t
-        done_w += enc["shape"][0] * enc["shape"][1]
-        if spent >= budget_s:
-            break
-    return done_w, spent
+    while True:
+        for enc, xs in mats_host:
+            t = time.perf_counter()
+            orc.c_decode_gemv(enc, xs, threads=threads)
+            spent += time.perf_counter() - t
+            done_w += enc["shape"][0] * enc["shape"][1]
+            if spent >= budget_s:
+                return done_w, spent
 
 
 def host_sample_matrices(cfg_name, n, seed_base=777):
@@ -267,8 +271,8 @@ def host_sample_matrices(cfg_name, n, seed_base=777):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=400)
+    ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="mine", choices=["mine", "reference"])
     ap.add_argument("--config", default="2", choices=sorted(CONFIGS))
     ap.add_argument("--layers", type=int, default=0, help="override layer count (0 = config's)")
@@ -296,7 +300,7 @@ def main():
         if rank != 0:
             return
         sample = host_sample_matrices(args.config, len(shapes))
-        per_step_budget = 3.0
+        per_step_budget = 2.0
         for _ in range(args.warmup):
             cpu_decode_gemv_sample(sample[:1], 0.0, ncores)
         w_tot, t_tot = 0, 0.0
@@ -372,16 +376,18 @@ def main():
             dist_.barrier()
         torch.cuda.synchronize()
 
+    clk = ClockSampler(torch.cuda.current_device() if world == 1 else local)
+    clk.start()
     for _ in range(args.warmup):
         one_step()
     barrier()
-    clk = ClockSampler(torch.cuda.current_device() if world == 1 else local)
-    clk.start()
+    time.sleep(0.5)          # nvidia-smi needs a moment before its first sample
     ev0 = torch.cuda.Event(enable_timing=True)
     ev1 = torch.cuda.Event(enable_timing=True)
     # kernel-only timing (same stream as the launches)
     kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     barrier()
+    t_wall0 = time.time()
     ev0.record(stream)
     for i in range(args.steps):
         kev[i][0].record(stream)
@@ -391,7 +397,7 @@ def main():
             gather()
     ev1.record(stream)
     barrier()
-    clocks = clk.stop()
+    clocks = clk.stop(t_wall0, time.time())
     t_ms = ev0.elapsed_time(ev1) / args.steps
     k_ms = sum(a.elapsed_time(b) for a, b in kev) / args.steps
     if world > 1:
@@ -460,7 +466,7 @@ def main():
             "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": traffic, "peak_kind": peak_kind,
                          "kernel": "gemv_step_kernel", "kernel_ms": round(k_ms, 4)},
-            "symbols_per_s": round(weights_step / (t_ms * 1e-3) / 1e12, 4),
+            "tsymbols_per_s": round(weights_step / (t_ms * 1e-3) / 1e12, 4),
             "gpu_launches": args.steps,
             "clocks": clocks,
             "e2e": {"value": round(e2e_val, 2), "unit": "GB/s", "ms_per_step": round(e2e_ms, 4),

@@ -25,6 +25,7 @@
 #include <cstdint>
 #include <cstdlib>
 #include <cstring>
+#include <algorithm>
 #include <vector>
 
 #include <cuda_bf16.h>
@@ -43,6 +44,9 @@ constexpr int kPadWords = 8;
 #endif
 #ifndef RB_STAGE_BYTES
 #define RB_STAGE_BYTES 8192
+#endif
+#ifndef RB_MINB
+#define RB_MINB 2        // 2 CTAs/SM: lets ptxas use up to 128 registers (no rematerialisation)
 #endif
 constexpr int kWarps = RB_WARPS;          // warps per CTA
 constexpr int kThreads = kWarps * 32;
@@ -75,6 +79,9 @@ struct Chunk {             // one CTA of the step launcher
 struct StepHeader {
     int ndesc, nchunks, R, pad_;
 };
+
+// The CTA's dynamic shared memory: [slot table 16 KB][per-warp stages].
+extern __shared__ __align__(16) uint8_t g_smem[];
 
 // ------------------------------------------------------------ primitives
 __device__ __forceinline__ void cp_async16(uint32_t saddr, const void* gptr) {
@@ -174,41 +181,137 @@ __device__ __forceinline__ uint64_t span_end(const MatDev& d, int64_t s_end) {
 // wb/pos: word base (shared stage or global words) and per-stream word index
 // of the stream's first (state) word.  NACC == 1: all streams share rows
 // (column mode, acc[0][r]); NACC == K: stream j owns acc[j] (row mode, shared x).
-template <int R, int K, int NACC, bool BF16X>
-__device__ __forceinline__ void decode_pass(const uint32_t* __restrict__ tab, const uint16_t* wb,
-                                            const uint32_t (&pos)[K], const int (&xcol)[K], int kk,
+// Word source of a pass.  Staged: `pos` are BYTE offsets into the CTA's
+// shared memory (the stage lives there), so a renormalisation read is one
+// LDS at [offset + array base] with no address arithmetic.  Global: `pos`
+// are word indices into d.words (spans too large to stage, or whose end is
+// unknown).
+template <bool STAGED>
+struct WordSrc;
+template <>
+struct WordSrc<true> {
+    static constexpr uint32_t kStep = 2;
+    __device__ __forceinline__ static uint32_t at(const MatDev&, uint32_t p) {
+        return *reinterpret_cast<const uint16_t*>(g_smem + p);
+    }
+};
+template <>
+struct WordSrc<false> {
+    static constexpr uint32_t kStep = 1;
+    __device__ __forceinline__ static uint32_t at(const MatDev& d, uint32_t p) { return __ldg(d.words + p); }
+};
+
+template <int K, int NACC, bool BF16X>
+__device__ __forceinline__ void load_xs(const MatDev& d, const int (&xcol)[K], int kk, int k, float (&xv)[K]) {
+    if (NACC == K) {
+        const float v = load_x<BF16X>(d, xcol[0] + 32 * k);
+#pragma unroll
+        for (int j = 0; j < K; ++j) xv[j] = v;
+    } else {
+#pragma unroll
+        for (int j = 0; j < K; ++j) xv[j] = (j < kk) ? load_x<BF16X>(d, xcol[j] + 32 * k) : 0.f;
+    }
+}
+
+#ifndef RB_INNER
+#define RB_INNER 1       // 0: C++ symbol step, 1: PTX symbol step, 2: PTX with mul.hi shifts
+#endif
+#ifndef RB_XPREF
+#define RB_XPREF 0
+#endif
+
+// One symbol of a staged stream, written in PTX so the instruction sequence
+// is fixed: table lookup (LDS), freq/bias fields, state update (IMAD),
+// predicated renormalisation (PRMT + pointer bump + LDS of the next word),
+// exact code value (PRMT + FADD) and the FMA.  st: state, w: next word,
+// pw: shared byte address of w, tb: shared address of the table.
+__device__ __forceinline__ void sym_step_ptx(uint32_t& st, uint32_t& w, uint32_t& pw, float& acc, float xv,
+                                             uint32_t tb) {
+#if RB_INNER == 2
+    asm("{\n\t.reg .pred p;\n\t.reg .b32 e, f, b, hi, a, c;\n\t"
+        "and.b32 a, %0, 4095;\n\t"
+        "shl.b32 a, a, 2;\n\t"
+        "add.u32 a, a, %5;\n\t"
+        "ld.shared.u32 e, [a];\n\t"
+        "mul.hi.u32 f, e, 4096;\n\t"
+        "shl.b32 b, e, 12;\n\t"
+        "mul.hi.u32 b, b, 4096;\n\t"
+        "mul.hi.u32 hi, %0, 1048576;\n\t"
+        "mad.lo.u32 %0, f, hi, b;\n\t"
+        "setp.lt.u32 p, %0, 65536;\n\t"
+        "@p prmt.b32 %0, %1, %0, 0x5410;\n\t"
+        "@p add.u32 %2, %2, 2;\n\t"
+        "@p ld.shared.u16 %1, [%2];\n\t"
+        "prmt.b32 c, e, 0x4B000000, 0x7540;\n\t"
+        "sub.f32 c, c, 0f4B000080;\n\t"
+        "fma.rn.f32 %3, c, %4, %3;\n\t}"
+        : "+r"(st), "+r"(w), "+r"(pw), "+f"(acc)
+        : "f"(xv), "r"(tb));
+#else
+    asm("{\n\t.reg .pred p;\n\t.reg .b32 e, f, b, hi, a, c;\n\t"
+        "and.b32 a, %0, 4095;\n\t"
+        "shl.b32 a, a, 2;\n\t"
+        "add.u32 a, a, %5;\n\t"
+        "ld.shared.u32 e, [a];\n\t"
+        "shr.u32 f, e, 20;\n\t"
+        "bfe.u32 b, e, 8, 12;\n\t"
+        "shr.u32 hi, %0, 12;\n\t"
+        "mad.lo.u32 %0, f, hi, b;\n\t"
+        "setp.lt.u32 p, %0, 65536;\n\t"
+        "@p prmt.b32 %0, %1, %0, 0x5410;\n\t"
+        "@p add.u32 %2, %2, 2;\n\t"
+        "@p ld.shared.u16 %1, [%2];\n\t"
+        "prmt.b32 c, e, 0x4B000000, 0x7540;\n\t"
+        "sub.f32 c, c, 0f4B000080;\n\t"
+        "fma.rn.f32 %3, c, %4, %3;\n\t}"
+        : "+r"(st), "+r"(w), "+r"(pw), "+f"(acc)
+        : "f"(xv), "r"(tb));
+#endif
+}
+
+template <int R, int K, int NACC, bool BF16X, bool STAGED>
+__device__ __forceinline__ void decode_pass(const uint32_t (&pos)[K], const int (&xcol)[K], int kk,
                                             const MatDev& d, float (&acc)[NACC][R], int& bad) {
+    using W = WordSrc<STAGED>;
+    const uint32_t* tab = reinterpret_cast<const uint32_t*>(g_smem);
+    const uint32_t tb = static_cast<uint32_t>(__cvta_generic_to_shared(g_smem));
     uint32_t st[K], w[K], p[K];
 #pragma unroll
     for (int j = 0; j < K; ++j) {
         p[j] = pos[j];
-        st[j] = (static_cast<uint32_t>(wb[p[j]]) << 16) | wb[p[j] + 1];
-        p[j] += 2;
-        w[j] = wb[p[j]];
+        st[j] = (W::at(d, p[j]) << 16) | W::at(d, p[j] + W::kStep);
+        p[j] += 2 * W::kStep;
+        w[j] = W::at(d, p[j]);
+        if (STAGED && RB_INNER != 0) p[j] += tb;   // absolute shared address for the PTX step
     }
     const int nk = d.nk;
+    float xn[K];
+    if (RB_XPREF) load_xs<K, NACC, BF16X>(d, xcol, kk, 0, xn);
     for (int k = 0; k < nk; ++k) {
         float xv[K];
-        if (NACC == K) {
-            const float v = load_x<BF16X>(d, xcol[0] + 32 * k);
+        if (RB_XPREF) {
 #pragma unroll
-            for (int j = 0; j < K; ++j) xv[j] = v;
+            for (int j = 0; j < K; ++j) xv[j] = xn[j];
+            if (k + 1 < nk) load_xs<K, NACC, BF16X>(d, xcol, kk, k + 1, xn);   // prefetch next k-step
         } else {
-#pragma unroll
-            for (int j = 0; j < K; ++j) xv[j] = (j < kk) ? load_x<BF16X>(d, xcol[j] + 32 * k) : 0.f;
+            load_xs<K, NACC, BF16X>(d, xcol, kk, k, xv);
         }
 #pragma unroll
         for (int r = 0; r < R; ++r) {
 #pragma unroll
             for (int j = 0; j < K; ++j) {
+                float& a = acc[NACC == 1 ? 0 : j][r];
+                if (STAGED && RB_INNER != 0) {
+                    sym_step_ptx(st[j], w[j], p[j], a, xv[j], tb);
+                    continue;
+                }
                 const uint32_t e = tab[st[j] & (kProbM - 1)];
                 st[j] = (e >> 20) * (st[j] >> kScaleBits) + ((e >> 8) & 0xFFFu);
                 if (st[j] < kRansL) {
                     st[j] = __byte_perm(w[j], st[j], 0x5410);
-                    ++p[j];
-                    w[j] = wb[p[j]];
+                    p[j] += W::kStep;
+                    w[j] = W::at(d, p[j]);
                 }
-                float& a = acc[NACC == 1 ? 0 : j][r];
                 a = fmaf(entry_code(e), xv[j], a);
             }
         }
@@ -221,7 +324,7 @@ __device__ __forceinline__ void decode_pass(const uint32_t* __restrict__ tab, co
 // Sets up a pass over tiles [t0, t0+kk) (consecutive), staging when possible,
 // and decodes it.  Streams j >= kk replay stream kk-1 with zero activation.
 template <int R, int K, int NACC, bool BF16X>
-__device__ __forceinline__ void run_pass(const MatDev& d, const uint32_t* tab, uint16_t* stage,
+__device__ __forceinline__ void run_pass(const MatDev& d, const uint32_t*, uint16_t* stage,
                                          int64_t t0, int kk, const int (&xcol)[K],
                                          float (&acc)[NACC][R], int& bad, int lane) {
     const int64_t s0 = t0 * 32;
@@ -232,12 +335,14 @@ __device__ __forceinline__ void run_pass(const MatDev& d, const uint32_t* tab, u
     for (int j = 0; j < K; ++j) pos[j] = d.offs[s0 + 32 * (j < kk ? j : kk - 1) + lane];
     if (kStageBytes > 0 && w1 != UINT64_MAX && staged_bytes(d, w0, w1) <= (uint64_t)kStageBytes) {
         const uint32_t head = stage_span(d, stage, w0, w1, lane);
+        // byte offset of the stage inside the CTA's shared memory
+        const uint32_t sbase = static_cast<uint32_t>(reinterpret_cast<uint8_t*>(stage) - g_smem);
 #pragma unroll
-        for (int j = 0; j < K; ++j) pos[j] = pos[j] - w0 + head;
-        decode_pass<R, K, NACC, BF16X>(tab, stage, pos, xcol, kk, d, acc, bad);
+        for (int j = 0; j < K; ++j) pos[j] = sbase + 2u * (pos[j] - w0 + head);
+        decode_pass<R, K, NACC, BF16X, true>(pos, xcol, kk, d, acc, bad);
         __syncwarp();   // stage is rewritten by the next pass
     } else {
-        decode_pass<R, K, NACC, BF16X>(tab, d.words, pos, xcol, kk, d, acc, bad);
+        decode_pass<R, K, NACC, BF16X, false>(pos, xcol, kk, d, acc, bad);
     }
 }
 
@@ -313,8 +418,8 @@ __device__ __forceinline__ void process_item(const MatDev& d, int item, const ui
 // ------------------------------------------------------------ kernels
 // One matrix: CTA b handles items [b*kWarps, b*kWarps + kWarps).
 template <int R, bool BF16X>
-__global__ void __launch_bounds__(kThreads) gemv_matrix_kernel(MatDev d) {
-    extern __shared__ __align__(16) uint8_t smem[];
+__global__ void __launch_bounds__(kThreads, RB_MINB) gemv_matrix_kernel(MatDev d) {
+    uint8_t* const smem = g_smem;
     uint32_t* tab = reinterpret_cast<uint32_t*>(smem);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     uint16_t* stage = reinterpret_cast<uint16_t*>(smem + kTableBytes + warp * kStageBytes);
@@ -328,8 +433,8 @@ __global__ void __launch_bounds__(kThreads) gemv_matrix_kernel(MatDev d) {
 
 // Every projection of a decoder step: CTA b processes chunk b (one matrix).
 template <int R>
-__global__ void __launch_bounds__(kThreads) gemv_step_kernel(const StepHeader* __restrict__ hdr) {
-    extern __shared__ __align__(16) uint8_t smem[];
+__global__ void __launch_bounds__(kThreads, RB_MINB) gemv_step_kernel(const StepHeader* __restrict__ hdr) {
+    uint8_t* const smem = g_smem;
     const MatDev* descs = reinterpret_cast<const MatDev*>(hdr + 1);
     const Chunk* chunks = reinterpret_cast<const Chunk*>(descs + hdr->ndesc);
     const Chunk ch = chunks[blockIdx.x];
@@ -351,7 +456,7 @@ __global__ void __launch_bounds__(kThreads) gemv_step_kernel(const StepHeader* _
 template <int R, int K>
 __global__ void __launch_bounds__(kThreads) decode_kernel(MatDev d, __nv_bfloat16* __restrict__ out,
                                                           int64_t ntiles) {
-    extern __shared__ __align__(16) uint8_t smem[];
+    uint8_t* const smem = g_smem;
     uint32_t* tab = reinterpret_cast<uint32_t*>(smem);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     uint16_t* stage = reinterpret_cast<uint16_t*>(smem + kTableBytes + warp * kStageBytes);
@@ -675,6 +780,14 @@ extern "C" int rans_gemv_step_plan(const RansGemvDesc* descs, int n, int R, void
             ++c;
         }
     }
+    // Longest chunks first: CTAs start in blockIdx order, so the grid's last
+    // wave holds the shortest chunks and the tail stays short.
+    auto item_cost = [&](const MatDev& d) -> int64_t {
+        return d.rowmode ? (int64_t)row_k(R) * R * d.cols : (int64_t)R * d.cbs * d.C;
+    };
+    std::stable_sort(ch, ch + nchunks, [&](const Chunk& a, const Chunk& b) {
+        return item_cost(md[a.desc]) > item_cost(md[b.desc]);
+    });
     if (grid_out) *grid_out = (int)nchunks;
     cudaError_t e = cudaMemcpyAsync(workspace, host.data(), host.size(), cudaMemcpyHostToDevice, stream);
     if (e != cudaSuccess) return (int)e;
