@@ -101,25 +101,6 @@ def make_step(cols, kind, seed):
     return (0.01 * rng.uniform(0.5, 1.5, cols)).astype(np.float32)
 
 
-def shard_encoding(enc, rank, world):
-    """Row-block shard [rb0, rb1) of an encoded matrix as a standalone encoding:
-    its streams are contiguous, so slice words/offs and rebase (no re-encode)."""
-    rows, cols = enc["shape"]
-    R, C = enc["R"], enc["C"]
-    nrb, ncb = rows // R, cols // C
-    rb0, rb1 = nrb * rank // world, nrb * (rank + 1) // world
-    s0, s1 = rb0 * ncb * 32, rb1 * ncb * 32
-    offs = enc["offs"].astype(np.int64)
-    w0 = int(offs[s0]) if s0 < offs.size else int(enc["words"].size) - 8
-    w0a = w0 - (w0 % 8)                      # keep 16-byte alignment of the slice
-    w1 = int(offs[s1]) if s1 < offs.size else int(enc["words"].size) - 8
-    words = np.zeros(w1 - w0a + 8, np.uint16)
-    words[: w1 - w0a] = enc["words"][w0a:w1]
-    out = dict(enc)
-    out.update(words=words, offs=(offs[s0:s1] - w0a).astype(np.uint32), shape=((rb1 - rb0) * R, cols))
-    return out, rb0 * R, (rb1 - rb0) * R
-
-
 def build_workload(torch, rb, cfg_name, layers, rank, world, device, log):
     shapes, nlayers, dist, bits, step_kind = CONFIGS[cfg_name]
     nlayers = layers if layers else nlayers
@@ -134,7 +115,7 @@ def build_workload(torch, rb, cfg_name, layers, rank, world, device, log):
             enc = rb.encode(codes, R_TILE, c_tile(cols), nthreads=nthreads)
             step = make_step(cols, step_kind, seed + 7)
             if world > 1:
-                enc, row0, nrows = shard_encoding(enc, rank, world)
+                enc, row0, nrows = rb.shard_encoding(enc, rank, world)
             else:
                 row0, nrows = 0, rows
             m = rb.RansMatrix(enc, torch.from_numpy(step), device=device)

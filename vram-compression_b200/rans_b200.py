@@ -183,6 +183,32 @@ def encode(codes, R: int, C: int, nthreads: int = 0) -> dict:
                 entropy_model=entropy_model)
 
 
+def shard_encoding(enc: dict, rank: int, world: int):
+    """Rank `rank`'s contiguous row-block range [rb0, rb1) of an encoded matrix,
+    as a standalone encoding of shape ((rb1-rb0)*R, cols).
+
+    Streams of consecutive row blocks are consecutive (stream = (rb*ncb+cb)*32
+    + lane), so the shard is a slice of offs and of words: no re-encoding.  The
+    word slice starts on an 8-word (16-byte) boundary and gets the 8 zero pad
+    words a standalone encoding ends with.  Returns (shard, first_row, nrows).
+    """
+    rows, cols = enc["shape"]
+    R, C = enc["R"], enc["C"]
+    nrb, ncb = rows // R, cols // C
+    rb0, rb1 = nrb * rank // world, nrb * (rank + 1) // world
+    s0, s1 = rb0 * ncb * 32, rb1 * ncb * 32
+    offs = np.asarray(enc["offs"]).astype(np.int64)
+    end = int(np.asarray(enc["words"]).size) - PAD_WORDS
+    w0 = int(offs[s0]) if s0 < offs.size else end
+    w1 = int(offs[s1]) if s1 < offs.size else end
+    w0a = w0 - (w0 % 8)
+    words = np.zeros(w1 - w0a + PAD_WORDS, np.uint16)
+    words[: w1 - w0a] = np.asarray(enc["words"])[w0a:w1]
+    out = dict(enc)
+    out.update(words=words, offs=(offs[s0:s1] - w0a).astype(np.uint32), shape=((rb1 - rb0) * R, cols))
+    return out, rb0 * R, (rb1 - rb0) * R
+
+
 # ------------------------------------------------------------------- device
 def _torch():
     import torch
