@@ -48,11 +48,21 @@ constexpr int kPadWords = 8;
 #ifndef RB_MINB
 #define RB_MINB 2        // 2 CTAs/SM: lets ptxas use up to 128 registers (no rematerialisation)
 #endif
+#ifndef RB_LAYOUT
+#define RB_LAYOUT 1      // shared-memory table entry: 0 = sym|bias<<8|freq<<20, 1 = bias|sym<<12|freq<<20
+#endif
+#ifndef RB_ALIGNTAB
+#define RB_ALIGNTAB 1    // place the table at a 16 KB-aligned shared address (address = one LOP3)
+#endif
 constexpr int kWarps = RB_WARPS;          // warps per CTA
 constexpr int kThreads = kWarps * 32;
 constexpr int kStageBytes = RB_STAGE_BYTES;  // per-warp staging buffer (0: no staging)
 constexpr int kTableBytes = kProbM * 4;
-constexpr int kSmemBytes = kTableBytes + kWarps * kStageBytes;
+constexpr int kAlignPad = RB_ALIGNTAB ? kTableBytes : 0;
+constexpr int kSmemBytes = kTableBytes + kWarps * kStageBytes + kAlignPad;
+// Layout 1 yields 4096*code from one LOP3; the sums are scaled back by 2^-12 (exact).
+constexpr float kCodeScale = RB_LAYOUT == 1 ? 4096.0f : 1.0f;
+constexpr float kInvCodeScale = 1.0f / kCodeScale;
 
 // Device view of one matrix plus its work decomposition.
 struct MatDev {
@@ -80,8 +90,29 @@ struct StepHeader {
     int ndesc, nchunks, R, pad_;
 };
 
-// The CTA's dynamic shared memory: [slot table 16 KB][per-warp stages].
+// The CTA's dynamic shared memory: the 16 KB slot table and one stage per
+// warp.  With RB_ALIGNTAB the table sits at the first 16 KB-aligned shared
+// address of the block, stages fill the space before and after it.
 extern __shared__ __align__(16) uint8_t g_smem[];
+
+struct SmemMap {
+    uint32_t* tab;       // generic pointer to the table
+    uint32_t tab_s;      // its shared-window address
+    uint16_t* stage;     // this warp's stage
+};
+
+__device__ __forceinline__ SmemMap smem_map(int warp) {
+    SmemMap m;
+    const uint32_t base = static_cast<uint32_t>(__cvta_generic_to_shared(g_smem));
+    const uint32_t toff = RB_ALIGNTAB ? ((uint32_t)kTableBytes - (base & (kTableBytes - 1))) & (kTableBytes - 1) : 0u;
+    m.tab = reinterpret_cast<uint32_t*>(g_smem + toff);
+    m.tab_s = base + toff;
+    const int nbefore = kStageBytes > 0 ? (int)(toff / kStageBytes) : 0;
+    const uint32_t soff = warp < nbefore ? (uint32_t)warp * kStageBytes
+                                         : toff + kTableBytes + (uint32_t)(warp - nbefore) * kStageBytes;
+    m.stage = reinterpret_cast<uint16_t*>(g_smem + soff);
+    return m;
+}
 
 // ------------------------------------------------------------ primitives
 __device__ __forceinline__ void cp_async16(uint32_t saddr, const void* gptr) {
@@ -90,18 +121,34 @@ __device__ __forceinline__ void cp_async16(uint32_t saddr, const void* gptr) {
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;\n" ::: "memory"); }
 
-// Reference table entry sym | freq<<8 | bias<<20  ->  sym | bias<<8 | freq<<20.
+// Reference table entry sym | freq<<8 | bias<<20 re-laid for the decoder.
 __device__ __forceinline__ uint32_t relayout_entry(uint32_t e) {
-    return (e & 0xFFu) | ((e >> 20) << 8) | (((e >> 8) & 0xFFFu) << 20);
+    const uint32_t sym = e & 0xFFu, freq = (e >> 8) & 0xFFFu, bias = e >> 20;
+#if RB_LAYOUT == 1
+    return bias | (sym << 12) | (freq << 20);
+#else
+    return sym | (bias << 8) | (freq << 20);
+#endif
 }
 
 __device__ __forceinline__ void load_table(uint32_t* tab, const uint32_t* __restrict__ table) {
     for (int i = threadIdx.x; i < (int)kProbM; i += blockDim.x) tab[i] = relayout_entry(__ldg(table + i));
 }
 
-// Signed code of a re-laid entry as an exact float: bits 0x4B0000ss = 2^23 + sym.
+__device__ __forceinline__ uint32_t entry_freq(uint32_t e) { return e >> 20; }
+__device__ __forceinline__ uint32_t entry_bias(uint32_t e) {
+    return RB_LAYOUT == 1 ? (e & 0xFFFu) : ((e >> 8) & 0xFFFu);
+}
+
+// kCodeScale * code as an exact float.  Layout 0: the float 2^23 + sym built
+// by one byte-permute, minus 2^23 + 128.  Layout 1: the float 2^23 + 4096*sym
+// (sym already sits at bits 12..19), minus 2^23 + 4096*128.
 __device__ __forceinline__ float entry_code(uint32_t e) {
+#if RB_LAYOUT == 1
+    return __int_as_float((e & 0x000FF000u) | 0x4B000000u) - 8912896.0f;
+#else
     return __int_as_float(__byte_perm(e, 0x4B000000u, 0x7540)) - 8388736.0f;
+#endif
 }
 
 template <bool BF16X>
@@ -222,29 +269,47 @@ __device__ __forceinline__ void load_xs(const MatDev& d, const int (&xcol)[K], i
 
 // One symbol of a staged stream, written in PTX so the instruction sequence
 // is fixed: table lookup (LDS), freq/bias fields, state update (IMAD),
-// predicated renormalisation (PRMT + pointer bump + LDS of the next word),
-// exact code value (PRMT + FADD) and the FMA.  st: state, w: next word,
-// pw: shared byte address of w, tb: shared address of the table.
+// predicated renormalisation (PRMT shift-in + pointer bump + LDS of the next
+// word), code value (one logic op + FADD) and the FMA.
+// st: state, w: next word, pw: shared byte address of w, tb: shared address
+// of the table (16 KB-aligned with RB_ALIGNTAB, so the entry address is
+// (st << 2 & 0x3ffc) | tb).
+#if RB_LAYOUT == 1
+#define RB_PTX_FIELDS                                  \
+    "shr.u32 f, e, 20;\n\t"                            \
+    "and.b32 b, e, 4095;\n\t"                          \
+    "shr.u32 hi, %0, 12;\n\t"                          \
+    "mad.lo.u32 %0, f, hi, b;\n\t"                     \
+    "setp.lt.u32 p, %0, 65536;\n\t"                    \
+    "@p prmt.b32 %0, %1, %0, 0x5410;\n\t"              \
+    "@p add.u32 %2, %2, 2;\n\t"                        \
+    "@p ld.shared.u16 %1, [%2];\n\t"                   \
+    "and.b32 c, e, 0x000FF000;\n\t"                    \
+    "or.b32 c, c, 0x4B000000;\n\t"                     \
+    "sub.f32 c, c, 0f4B080000;\n\t"                    \
+    "fma.rn.f32 %3, c, %4, %3;\n\t}"
+#else
+#define RB_PTX_FIELDS                                  \
+    "shr.u32 f, e, 20;\n\t"                            \
+    "bfe.u32 b, e, 8, 12;\n\t"                         \
+    "shr.u32 hi, %0, 12;\n\t"                          \
+    "mad.lo.u32 %0, f, hi, b;\n\t"                     \
+    "setp.lt.u32 p, %0, 65536;\n\t"                    \
+    "@p prmt.b32 %0, %1, %0, 0x5410;\n\t"              \
+    "@p add.u32 %2, %2, 2;\n\t"                        \
+    "@p ld.shared.u16 %1, [%2];\n\t"                   \
+    "prmt.b32 c, e, 0x4B000000, 0x7540;\n\t"           \
+    "sub.f32 c, c, 0f4B000080;\n\t"                    \
+    "fma.rn.f32 %3, c, %4, %3;\n\t}"
+#endif
 __device__ __forceinline__ void sym_step_ptx(uint32_t& st, uint32_t& w, uint32_t& pw, float& acc, float xv,
                                              uint32_t tb) {
-#if RB_INNER == 2
+#if RB_ALIGNTAB
     asm("{\n\t.reg .pred p;\n\t.reg .b32 e, f, b, hi, a, c;\n\t"
-        "and.b32 a, %0, 4095;\n\t"
-        "shl.b32 a, a, 2;\n\t"
-        "add.u32 a, a, %5;\n\t"
-        "ld.shared.u32 e, [a];\n\t"
-        "mul.hi.u32 f, e, 4096;\n\t"
-        "shl.b32 b, e, 12;\n\t"
-        "mul.hi.u32 b, b, 4096;\n\t"
-        "mul.hi.u32 hi, %0, 1048576;\n\t"
-        "mad.lo.u32 %0, f, hi, b;\n\t"
-        "setp.lt.u32 p, %0, 65536;\n\t"
-        "@p prmt.b32 %0, %1, %0, 0x5410;\n\t"
-        "@p add.u32 %2, %2, 2;\n\t"
-        "@p ld.shared.u16 %1, [%2];\n\t"
-        "prmt.b32 c, e, 0x4B000000, 0x7540;\n\t"
-        "sub.f32 c, c, 0f4B000080;\n\t"
-        "fma.rn.f32 %3, c, %4, %3;\n\t}"
+        "shl.b32 a, %0, 2;\n\t"
+        "and.b32 a, a, 0x3FFC;\n\t"
+        "or.b32 a, a, %5;\n\t"
+        "ld.shared.u32 e, [a];\n\t" RB_PTX_FIELDS
         : "+r"(st), "+r"(w), "+r"(pw), "+f"(acc)
         : "f"(xv), "r"(tb));
 #else
@@ -252,18 +317,7 @@ __device__ __forceinline__ void sym_step_ptx(uint32_t& st, uint32_t& w, uint32_t
         "and.b32 a, %0, 4095;\n\t"
         "shl.b32 a, a, 2;\n\t"
         "add.u32 a, a, %5;\n\t"
-        "ld.shared.u32 e, [a];\n\t"
-        "shr.u32 f, e, 20;\n\t"
-        "bfe.u32 b, e, 8, 12;\n\t"
-        "shr.u32 hi, %0, 12;\n\t"
-        "mad.lo.u32 %0, f, hi, b;\n\t"
-        "setp.lt.u32 p, %0, 65536;\n\t"
-        "@p prmt.b32 %0, %1, %0, 0x5410;\n\t"
-        "@p add.u32 %2, %2, 2;\n\t"
-        "@p ld.shared.u16 %1, [%2];\n\t"
-        "prmt.b32 c, e, 0x4B000000, 0x7540;\n\t"
-        "sub.f32 c, c, 0f4B000080;\n\t"
-        "fma.rn.f32 %3, c, %4, %3;\n\t}"
+        "ld.shared.u32 e, [a];\n\t" RB_PTX_FIELDS
         : "+r"(st), "+r"(w), "+r"(pw), "+f"(acc)
         : "f"(xv), "r"(tb));
 #endif
@@ -273,8 +327,9 @@ template <int R, int K, int NACC, bool BF16X, bool STAGED>
 __device__ __forceinline__ void decode_pass(const uint32_t (&pos)[K], const int (&xcol)[K], int kk,
                                             const MatDev& d, float (&acc)[NACC][R], int& bad) {
     using W = WordSrc<STAGED>;
-    const uint32_t* tab = reinterpret_cast<const uint32_t*>(g_smem);
-    const uint32_t tb = static_cast<uint32_t>(__cvta_generic_to_shared(g_smem));
+    const SmemMap sm = smem_map(0);
+    const uint32_t* tab = sm.tab;
+    const uint32_t tb = sm.tab_s;
     uint32_t st[K], w[K], p[K];
 #pragma unroll
     for (int j = 0; j < K; ++j) {
@@ -282,7 +337,8 @@ __device__ __forceinline__ void decode_pass(const uint32_t (&pos)[K], const int 
         st[j] = (W::at(d, p[j]) << 16) | W::at(d, p[j] + W::kStep);
         p[j] += 2 * W::kStep;
         w[j] = W::at(d, p[j]);
-        if (STAGED && RB_INNER != 0) p[j] += tb;   // absolute shared address for the PTX step
+        // absolute shared address (offset from g_smem + its window address) for the PTX step
+        if (STAGED && RB_INNER != 0) p[j] += static_cast<uint32_t>(__cvta_generic_to_shared(g_smem));
     }
     const int nk = d.nk;
     float xn[K];
@@ -306,7 +362,7 @@ __device__ __forceinline__ void decode_pass(const uint32_t (&pos)[K], const int 
                     continue;
                 }
                 const uint32_t e = tab[st[j] & (kProbM - 1)];
-                st[j] = (e >> 20) * (st[j] >> kScaleBits) + ((e >> 8) & 0xFFFu);
+                st[j] = entry_freq(e) * (st[j] >> kScaleBits) + entry_bias(e);
                 if (st[j] < kRansL) {
                     st[j] = __byte_perm(w[j], st[j], 0x5410);
                     p[j] += W::kStep;
@@ -364,7 +420,7 @@ __device__ void colmode_item(const MatDev& d, int item, const uint32_t* tab, uin
         for (int j = 0; j < K; ++j) xcol[j] = (cb0 + (j < kk ? j : 0)) * d.C + lane;
         run_pass<R, K, 1, BF16X>(d, tab, stage, (int64_t)rb * d.ncb + cb0, kk, xcol, acc, bad, lane);
     }
-    const float s = reduce_scatter<R>(acc[0], lane);
+    const float s = reduce_scatter<R>(acc[0], lane) * kInvCodeScale;
     constexpr int kShift = 5 - Log2<R>::value;
     if ((lane & ((1 << kShift) - 1)) == 0) {
         const int row = rb * R + (lane >> kShift);
@@ -392,7 +448,7 @@ __device__ void rowmode_item(const MatDev& d, int item, const uint32_t* tab, uin
     float v[KR * R];
 #pragma unroll
     for (int i = 0; i < KR * R; ++i) v[i] = flat[i];
-    const float s = reduce_scatter<KR * R>(v, lane);
+    const float s = reduce_scatter<KR * R>(v, lane) * kInvCodeScale;
     constexpr int kShift = 5 - Log2<KR * R>::value;
     const int idx = lane >> kShift;          // = j*R + r
     if ((lane & ((1 << kShift) - 1)) == 0 && idx / R < kk) d.y[(rb0 + idx / R) * R + idx % R] = s;
@@ -419,10 +475,10 @@ __device__ __forceinline__ void process_item(const MatDev& d, int item, const ui
 // One matrix: CTA b handles items [b*kWarps, b*kWarps + kWarps).
 template <int R, bool BF16X>
 __global__ void __launch_bounds__(kThreads, RB_MINB) gemv_matrix_kernel(MatDev d) {
-    uint8_t* const smem = g_smem;
-    uint32_t* tab = reinterpret_cast<uint32_t*>(smem);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    uint16_t* stage = reinterpret_cast<uint16_t*>(smem + kTableBytes + warp * kStageBytes);
+    const SmemMap sm = smem_map(warp);
+    uint32_t* tab = sm.tab;
+    uint16_t* stage = sm.stage;
     load_table(tab, d.table);
     __syncthreads();
     const int item = blockIdx.x * kWarps + warp;
@@ -434,14 +490,14 @@ __global__ void __launch_bounds__(kThreads, RB_MINB) gemv_matrix_kernel(MatDev d
 // Every projection of a decoder step: CTA b processes chunk b (one matrix).
 template <int R>
 __global__ void __launch_bounds__(kThreads, RB_MINB) gemv_step_kernel(const StepHeader* __restrict__ hdr) {
-    uint8_t* const smem = g_smem;
     const MatDev* descs = reinterpret_cast<const MatDev*>(hdr + 1);
     const Chunk* chunks = reinterpret_cast<const Chunk*>(descs + hdr->ndesc);
     const Chunk ch = chunks[blockIdx.x];
     const MatDev& d = descs[ch.desc];
-    uint32_t* tab = reinterpret_cast<uint32_t*>(smem);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    uint16_t* stage = reinterpret_cast<uint16_t*>(smem + kTableBytes + warp * kStageBytes);
+    const SmemMap sm = smem_map(warp);
+    uint32_t* tab = sm.tab;
+    uint16_t* stage = sm.stage;
     load_table(tab, d.table);
     __syncthreads();
     if (warp >= ch.nitems) return;
@@ -456,10 +512,10 @@ __global__ void __launch_bounds__(kThreads, RB_MINB) gemv_step_kernel(const Step
 template <int R, int K>
 __global__ void __launch_bounds__(kThreads) decode_kernel(MatDev d, __nv_bfloat16* __restrict__ out,
                                                           int64_t ntiles) {
-    uint8_t* const smem = g_smem;
-    uint32_t* tab = reinterpret_cast<uint32_t*>(smem);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    uint16_t* stage = reinterpret_cast<uint16_t*>(smem + kTableBytes + warp * kStageBytes);
+    const SmemMap sm = smem_map(warp);
+    uint32_t* tab = sm.tab;
+    uint16_t* stage = sm.stage;
     load_table(tab, d.table);
     __syncthreads();
     const int64_t t0 = ((int64_t)blockIdx.x * kWarps + warp) * K;
@@ -500,13 +556,13 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(MatDev d, __nv_bfloat1
         for (int k = 0; k < d.nk; ++k) {
             float sv[K];
 #pragma unroll
-            for (int j = 0; j < K; ++j) sv[j] = __ldg(d.step + cbase[j] + 32 * k);
+            for (int j = 0; j < K; ++j) sv[j] = __ldg(d.step + cbase[j] + 32 * k) * kInvCodeScale;
 #pragma unroll
             for (int r = 0; r < R; ++r) {
 #pragma unroll
                 for (int j = 0; j < K; ++j) {
                     const uint32_t e = tab[st[j] & (kProbM - 1)];
-                    st[j] = (e >> 20) * (st[j] >> kScaleBits) + ((e >> 8) & 0xFFFu);
+                    st[j] = entry_freq(e) * (st[j] >> kScaleBits) + entry_bias(e);
                     if (st[j] < kRansL) {
                         st[j] = __byte_perm(w[j], st[j], 0x5410);
                         ++p[j];
