@@ -110,6 +110,23 @@ int rans_gemv_step_plan(const RansGemvDesc* descs, int n, int R, void* workspace
  * matrix (kernel/bench.py:104-107, kernel/rans.py:147-151). */
 int rans_gemv_step_launch(int R, const void* workspace, int grid, cudaStream_t stream);
 
+/* The same decoder step for callers that cannot allocate device memory when
+ * they run it: a framework whose caching allocator owns the whole pool (a
+ * private cudaMalloc would fragment it or fail under pressure), an inference
+ * loop that forbids allocation after start-up, a runtime without an allocator
+ * handle to hand over.  It plans and launches in one call and allocates
+ * nothing: the plan goes to a 256 KB file-scope device array that every GPU
+ * loading this library holds until exit.  `descs` is a HOST array of device
+ * pointers, as for rans_gemv_step_plan.  Returns -3 when the plan of these
+ * descriptors exceeds 256 KB (about 14,000 eight-warp chunks, e.g. one
+ * Qwen2.5-1.5B decoder step; split larger steps into several calls).
+ * The first call on a device looks up the array's device address with that
+ * device current; make that first call before any stream capture.  All calls
+ * share the one array and it keeps the last call's plan: calls whose work
+ * overlaps on the GPU (different streams, or graphs replaying one call while
+ * another plans) race.  No counterpart in the reference. */
+int rans_gemv_step_noalloc(const RansGemvDesc* descs, int n, int R, cudaStream_t stream);
+
 /* ------------------------------------------------------------ host encoder
  * Bit-exact C++ restatement of the reference producer kernel/rans.py:34-98
  * (build_table, lane_order, encode), multithreaded over tiles.            */

@@ -26,6 +26,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <algorithm>
+#include <mutex>
 #include <vector>
 
 #include <cuda_bf16.h>
@@ -871,6 +872,90 @@ extern "C" int rans_gemv_step_launch(int R, const void* workspace, int grid, cud
         case 16: return launch_step_t<16>(workspace, nchunks, stream);
         default: return -1;
     }
+}
+
+// ------------------------------------------------- step launcher, no allocation
+// Some callers cannot allocate device memory at the point where they run a
+// decoder step: a framework whose caching allocator owns the whole pool (a
+// private cudaMalloc behind its back fragments it, or fails under memory
+// pressure), an inference loop that forbids allocation after start-up to keep
+// its latency predictable, or a runtime with no allocator handle to give us.
+// rans_gemv_step_noalloc serves them: the work plan that rans_gemv_step_plan
+// writes into a caller-allocated workspace lives here in a fixed-size
+// file-scope device array instead.
+constexpr size_t kNoAllocScratchBytes = 256 * 1024;   // the plan's maximum size
+constexpr int kNoAllocMaxDevices = 64;
+
+static __device__ __align__(256) uint8_t g_step_scratch[kNoAllocScratchBytes];
+
+// Host staging of the plan (static: no heap) and, per device, the device
+// address of g_step_scratch (the host-side name is only a stand-in).
+static uint8_t g_noalloc_host[kNoAllocScratchBytes];
+static void* g_noalloc_dev[kNoAllocMaxDevices];
+static std::mutex g_noalloc_mu;
+
+extern "C" int rans_gemv_step_noalloc(const RansGemvDesc* descs, int n, int R, cudaStream_t stream) {
+    if (!valid_R(R)) return -1;
+    if (n <= 0 || descs == nullptr) return -2;
+    // size check from the shapes alone, before touching any device state
+    int64_t nchunks = 0;
+    for (int i = 0; i < n; ++i) {
+        const RansGemvDesc& s = descs[i];
+        if (!shape_ok(R, s.rows, s.cols, s.C)) return -2;
+        MatDev d = make_desc(s.words, s.offs, s.table, s.x, s.step, s.y, s.rows, s.cols, s.C, s.nwords);
+        plan_matrix(d, R, 0);
+        nchunks += (d.nitems + kWarps - 1) / kWarps;
+    }
+    const size_t bytes = step_bytes(n, nchunks);
+    if (bytes > kNoAllocScratchBytes) return -3;   // plan larger than the static scratch
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return (int)e;
+    if (dev < 0 || dev >= kNoAllocMaxDevices) return -2;
+    if (g_noalloc_dev[dev] == nullptr) {
+        // once per device, with that device current
+        void* p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_step_scratch);
+        if (e != cudaSuccess) return (int)e;
+        g_noalloc_dev[dev] = p;
+    }
+    StepHeader* h = reinterpret_cast<StepHeader*>(g_noalloc_host);
+    h->ndesc = n;
+    h->nchunks = (int)nchunks;
+    h->R = R;
+    h->pad_ = 0;
+    MatDev* md = reinterpret_cast<MatDev*>(h + 1);
+    Chunk* ch = reinterpret_cast<Chunk*>(md + n);
+    int64_t c = 0;
+    for (int i = 0; i < n; ++i) {
+        const RansGemvDesc& s = descs[i];
+        md[i] = make_desc(s.words, s.offs, s.table, s.x, s.step, s.y, s.rows, s.cols, s.C, s.nwords);
+        plan_matrix(md[i], R, 0);
+        for (int it = 0; it < md[i].nitems; it += kWarps) {
+            ch[c].desc = i;
+            ch[c].item0 = it;
+            ch[c].nitems = md[i].nitems - it < kWarps ? md[i].nitems - it : kWarps;
+            ch[c].pad_ = 0;
+            ++c;
+        }
+    }
+    // same order as rans_gemv_step_plan (longest chunks first, ties in input
+    // order), with an in-place sort
+    auto item_cost = [&](const MatDev& d) -> int64_t {
+        return d.rowmode ? (int64_t)row_k(R) * R * d.cols : (int64_t)R * d.cbs * d.C;
+    };
+    std::sort(ch, ch + nchunks, [&](const Chunk& a, const Chunk& b) {
+        const int64_t ca = item_cost(md[a.desc]), cb = item_cost(md[b.desc]);
+        if (ca != cb) return ca > cb;
+        if (a.desc != b.desc) return a.desc < b.desc;
+        return a.item0 < b.item0;
+    });
+    // A pageable-source copy returns once the bytes are staged, so the static
+    // host buffer may be rewritten by the next call.
+    e = cudaMemcpyAsync(g_noalloc_dev[dev], g_noalloc_host, bytes, cudaMemcpyHostToDevice, stream);
+    if (e != cudaSuccess) return (int)e;
+    return rans_gemv_step_launch(R, g_noalloc_dev[dev], (int)nchunks, stream);
 }
 
 extern "C" int rans_b200_abi_version(void) { return RANS_B200_ABI_VERSION; }
