@@ -259,6 +259,9 @@ def main():
     ap.add_argument("--layers", type=int, default=0, help="override layer count (0 = config's)")
     ap.add_argument("--cpu-budget", type=float, default=12.0, help="seconds of CPU-baseline work")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--exchange", default="fused", choices=["fused", "nccl"],
+                    help="N>1: outputs written to every rank by the kernel (fused) or NCCL all-gather per layer")
+    ap.add_argument("--check", action="store_true", help="N>1: verify the fused exchange against NCCL")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -319,22 +322,44 @@ def main():
     rb.load()
 
     mats, meta = build_workload(torch, rb, args.config, nlayers, rank, world, device, log)
-    # one contiguous activation / output buffer for the whole step
+    # one contiguous activation buffer for the whole step
     xsz = [m.cols for m in mats]
     ysz = [m.rows for m in mats]
     x_all = torch.randn(sum(xsz), generator=torch.Generator(device=device).manual_seed(99),
                         device=device).to(torch.bfloat16)
-    y_all = torch.zeros(sum(ysz), device=device)
     xs = list(torch.split(x_all, xsz))
-    ys = list(torch.split(y_all, ysz))
-    step = rb.RansStep(mats, xs, ys)
     stream = torch.cuda.current_stream()
-
+    per_layer = len(shapes)
     gather = None
-    if world > 1:
+    hdl = None
+    if world > 1 and args.exchange == "fused":
+        # every rank holds the FULL outputs of every projection in symmetric
+        # memory; the kernel stores its shard rows into all ranks' copies
+        import torch.distributed as dist_
+        import torch.distributed._symmetric_memory as symm_mem
+        full = [m["rows"] for m in meta]
+        F = np.concatenate([[0], np.cumsum(full)[:-1]]).astype(np.int64)
+        y_all = symm_mem.empty(int(sum(full)), dtype=torch.float32, device=device)
+        y_all.zero_()
+        try:
+            hdl = symm_mem.rendezvous(y_all, dist_.group.WORLD)
+        except Exception:
+            symm_mem.enable_symm_mem_for_group(dist_.group.WORLD.group_name)
+            hdl = symm_mem.rendezvous(y_all, dist_.group.WORLD)
+        ptrs = [int(p) for p in hdl.buffer_ptrs]
+        ys = [y_all[int(F[i]) + m["row0"]: int(F[i]) + m["row0"] + m["nrows"]] for i, m in enumerate(meta)]
+        peers = [[ptrs[p] + 4 * (int(F[i]) + m["row0"]) for p in range(world)] for i, m in enumerate(meta)]
+        step = rb.RansStep(mats, xs, ys, peers=peers)
+
+        def gather():
+            hdl.barrier(channel=0, timeout_ms=60000)
+    else:
+        y_all = torch.zeros(sum(ysz), device=device)
+        ys = list(torch.split(y_all, ysz))
+        step = rb.RansStep(mats, xs, ys)
+    if world > 1 and args.exchange == "nccl":
         import torch.distributed as dist_
         # per layer: all-gather every rank's shard outputs of the layer's projections
-        per_layer = len(shapes)
         layer_rows = [sum(ysz[i * per_layer:(i + 1) * per_layer]) for i in range(nlayers)]
         gbufs = [torch.empty(world * max(layer_rows), device=device) for _ in range(nlayers)]
         starts = np.cumsum([0] + ysz)
@@ -386,6 +411,28 @@ def main():
         tt = torch.tensor([t_ms, k_ms], device=device)
         dist_.all_reduce(tt, op=dist_.ReduceOp.MAX)
         t_ms, k_ms = tt.tolist()
+
+    exchange_check = None
+    if world > 1 and args.check and args.exchange == "fused":
+        # same shards through the plain plan, gathered by NCCL, must equal the fused exchange
+        import torch.distributed as dist_
+        y_plain = torch.zeros(sum(ysz), device=device)
+        ref_step = rb.RansStep(mats, xs, list(torch.split(y_plain, ysz)))
+        ref_step()
+        step()
+        gather()
+        torch.cuda.synchronize()
+        worst = 0.0
+        off = 0
+        for i, m in enumerate(meta):
+            gathered = torch.empty(world * m["nrows"], device=device)
+            dist_.all_gather_into_tensor(gathered, y_plain[off: off + m["nrows"]])
+            full_i = y_all[int(F[i]): int(F[i]) + m["rows"]]
+            worst = max(worst, (gathered - full_i).abs().max().item())
+            off += m["nrows"]
+        t = torch.tensor([worst], device=device)
+        dist_.all_reduce(t, op=dist_.ReduceOp.MAX)
+        exchange_check = {"max_abs_diff_vs_nccl_allgather": t.item(), "ok": t.item() == 0.0}
 
     # end to end through the public API: pinned host x -> device, step, y -> pinned host
     x_host = x_all.cpu().pin_memory()
@@ -454,6 +501,13 @@ def main():
                     "h2d_bytes_per_step": int(x_all.numel() * 2), "d2h_bytes_per_step": int(y_all.numel() * 4)},
             "cpu_baseline": cpu,
         }
+        if world > 1:
+            line["exchange"] = {"kind": args.exchange,
+                                "how": ("kernel epilogue stores each output row into every rank's output "
+                                        "buffer (symmetric memory over NVLink) + one cross-GPU barrier per step"
+                                        if args.exchange == "fused" else
+                                        "NCCL all_gather_into_tensor per layer after the step kernel"),
+                                "check": exchange_check}
         print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist_

@@ -103,6 +103,19 @@ int64_t rans_gemv_step_workspace_bytes(const RansGemvDesc* descs, int n, int R);
 int rans_gemv_step_plan(const RansGemvDesc* descs, int n, int R, void* workspace,
                         size_t workspace_bytes, int* grid_out, cudaStream_t stream);
 
+/* Row-sharded multi-GPU variant of rans_gemv_step_plan: descs[i] describes
+ * this rank's row shard of projection i, and peer_y[i*npeers + p] is the
+ * device address (valid on this GPU: NVLink peer mapping / symmetric memory)
+ * of the first row of that shard inside rank p's FULL output buffer of
+ * projection i, this rank included.  The kernel then stores every output row
+ * to all npeers buffers (the all-gather of the outputs is fused into the
+ * epilogue; npeers <= 8, one node) and fences at system scope; the caller
+ * runs one cross-GPU barrier after the launch before reading outputs.
+ * Replaces the reference's (absent) exchange; no counterpart there. */
+int rans_gemv_step_plan_peers(const RansGemvDesc* descs, const void* const* peer_y, int npeers,
+                              int n, int R, void* workspace, size_t workspace_bytes,
+                              int* grid_out, cudaStream_t stream);
+
 /* Run every projection of a decoder step from ONE grid (one kernel launch,
  * capturable in a CUDA graph).  Each CTA loads the slot table of its matrix
  * and its warps decode whole row blocks, so y is stored without atomics.

@@ -65,6 +65,8 @@ constexpr int kSmemBytes = kTableBytes + kWarps * kStageBytes + kAlignPad;
 constexpr float kCodeScale = RB_LAYOUT == 1 ? 4096.0f : 1.0f;
 constexpr float kInvCodeScale = 1.0f / kCodeScale;
 
+constexpr int kMaxPeers = 8;              // ranks of one NVLink/NVSwitch node
+
 // Device view of one matrix plus its work decomposition.
 struct MatDev {
     const uint16_t* words;
@@ -80,7 +82,9 @@ struct MatDev {
     int nseg, cbs;         // column-mode segments per row block, cbs per segment
     int nitems;
     int accumulate;        // 1: atomicAdd into y (split rows), 0: store
-    int pad_[3];
+    int npeer;             // > 0: store every output row to all of ypeer[] instead of y
+    int pad_[2];
+    float* ypeer[kMaxPeers];   // the same rows of every rank's output buffer (peer addresses)
 };
 
 struct Chunk {             // one CTA of the step launcher
@@ -403,6 +407,17 @@ __device__ __forceinline__ void run_pass(const MatDev& d, const uint32_t*, uint1
     }
 }
 
+// Fused output exchange of the row-sharded path: the row goes to every rank's
+// output buffer (plain stores over NVLink; ypeer[] includes this rank's own
+// buffer), followed by a system-scope fence so the stores are performed
+// before the cross-GPU barrier that follows the kernel.
+__device__ __forceinline__ void store_peers(const MatDev& d, int row, float s) {
+#pragma unroll
+    for (int p = 0; p < kMaxPeers; ++p)
+        if (p < d.npeer) d.ypeer[p][row] = s;
+    __threadfence_system();
+}
+
 // Column mode: rows rb*R..rb*R+R-1, column blocks of segment `seg`.
 template <int R, int K, bool BF16X>
 __device__ void colmode_item(const MatDev& d, int item, const uint32_t* tab, uint16_t* stage,
@@ -426,6 +441,7 @@ __device__ void colmode_item(const MatDev& d, int item, const uint32_t* tab, uin
     if ((lane & ((1 << kShift) - 1)) == 0) {
         const int row = rb * R + (lane >> kShift);
         if (d.accumulate) atomicAdd(d.y + row, s);
+        else if (d.npeer > 0) store_peers(d, row, s);
         else d.y[row] = s;
     }
 }
@@ -452,7 +468,11 @@ __device__ void rowmode_item(const MatDev& d, int item, const uint32_t* tab, uin
     const float s = reduce_scatter<KR * R>(v, lane) * kInvCodeScale;
     constexpr int kShift = 5 - Log2<KR * R>::value;
     const int idx = lane >> kShift;          // = j*R + r
-    if ((lane & ((1 << kShift) - 1)) == 0 && idx / R < kk) d.y[(rb0 + idx / R) * R + idx % R] = s;
+    if ((lane & ((1 << kShift) - 1)) == 0 && idx / R < kk) {
+        const int row = (rb0 + idx / R) * R + idx % R;
+        if (d.npeer > 0) store_peers(d, row, s);
+        else d.y[row] = s;
+    }
 }
 
 template <int R>
@@ -811,13 +831,34 @@ extern "C" int64_t rans_gemv_step_workspace_bytes(const RansGemvDesc* descs, int
     return (int64_t)step_bytes(n, nchunks);
 }
 
+static int plan_step(const RansGemvDesc* descs, const void* const* peer_y, int npeers, int n, int R,
+                     void* workspace, size_t workspace_bytes, int* grid_out, cudaStream_t stream);
+
 extern "C" int rans_gemv_step_plan(const RansGemvDesc* descs, int n, int R, void* workspace,
                                    size_t workspace_bytes, int* grid_out, cudaStream_t stream) {
+    return plan_step(descs, nullptr, 0, n, R, workspace, workspace_bytes, grid_out, stream);
+}
+
+extern "C" int rans_gemv_step_plan_peers(const RansGemvDesc* descs, const void* const* peer_y, int npeers,
+                                         int n, int R, void* workspace, size_t workspace_bytes,
+                                         int* grid_out, cudaStream_t stream) {
+    if (npeers < 1 || npeers > kMaxPeers || peer_y == nullptr) return -2;
+    return plan_step(descs, peer_y, npeers, n, R, workspace, workspace_bytes, grid_out, stream);
+}
+
+static int plan_step(const RansGemvDesc* descs, const void* const* peer_y, int npeers, int n, int R,
+                     void* workspace, size_t workspace_bytes, int* grid_out, cudaStream_t stream) {
     if (!valid_R(R)) return -1;
     if (n <= 0) return -2;
     std::vector<MatDev> mats;
     const int64_t nchunks = count_chunks(descs, n, R, &mats);
     if (nchunks < 0) return -2;
+    for (int i = 0; i < n && peer_y != nullptr; ++i) {
+        if (mats[i].accumulate) return -2;   // split rows cannot be exchanged by stores
+        mats[i].npeer = npeers;
+        for (int p = 0; p < npeers; ++p)
+            mats[i].ypeer[p] = static_cast<float*>(const_cast<void*>(peer_y[(size_t)i * npeers + p]));
+    }
     if (step_bytes(n, nchunks) > workspace_bytes) return -3;
     std::vector<uint8_t> host(step_bytes(n, nchunks));
     StepHeader* h = reinterpret_cast<StepHeader*>(host.data());

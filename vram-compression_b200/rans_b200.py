@@ -56,6 +56,8 @@ def _bind(lib):
     lib.rans_gemv_step_workspace_bytes.restype = _i64
     lib.rans_gemv_step_plan.argtypes = [_vp, _i32, _i32, _vp, _sz, _vp, _vp]
     lib.rans_gemv_step_plan.restype = _i32
+    lib.rans_gemv_step_plan_peers.argtypes = [_vp, _vp, _i32, _i32, _i32, _vp, _sz, _vp, _vp]
+    lib.rans_gemv_step_plan_peers.restype = _i32
     lib.rans_gemv_step_launch.argtypes = [_i32, _vp, _i32, _vp]
     lib.rans_gemv_step_launch.restype = _i32
     lib.rans_build_table_host.argtypes = [_vp, _i64, _vp, _vp, _vp, _i32]
@@ -323,7 +325,10 @@ class RansStep:
     The plan is built once; __call__ is a single asynchronous launch.
     """
 
-    def __init__(self, mats, xs, ys, lib=None):
+    def __init__(self, mats, xs, ys, lib=None, peers=None):
+        """peers: optional, per matrix the device addresses (valid on this GPU)
+        of the matching rows in every rank's output buffer; the kernel then
+        writes each output row to all of them (fused all-gather)."""
         torch = _torch()
         self.lib = _lib(lib)
         if not mats:
@@ -340,9 +345,20 @@ class RansStep:
             raise ValueError(f"bad step description ({nbytes})")
         self.workspace = torch.empty(int(nbytes), dtype=torch.uint8, device=mats[0].device)
         grid = ctypes.c_int(0)
-        rc = self.lib.rans_gemv_step_plan(ctypes.addressof(arr), len(mats), R, self.workspace.data_ptr(),
-                                          int(nbytes), ctypes.byref(grid), _stream(torch))
-        _check(rc, "rans_gemv_step_plan")
+        if peers is None:
+            rc = self.lib.rans_gemv_step_plan(ctypes.addressof(arr), len(mats), R, self.workspace.data_ptr(),
+                                              int(nbytes), ctypes.byref(grid), _stream(torch))
+            _check(rc, "rans_gemv_step_plan")
+        else:
+            npeers = len(peers[0])
+            if len(peers) != len(mats) or any(len(p) != npeers for p in peers):
+                raise ValueError("peers must list the same number of ranks for every matrix")
+            flat = (ctypes.c_void_p * (len(mats) * npeers))(*[int(a) for p in peers for a in p])
+            self._peer_arr = flat
+            rc = self.lib.rans_gemv_step_plan_peers(ctypes.addressof(arr), ctypes.addressof(flat), npeers,
+                                                    len(mats), R, self.workspace.data_ptr(), int(nbytes),
+                                                    ctypes.byref(grid), _stream(torch))
+            _check(rc, "rans_gemv_step_plan_peers")
         self.grid = grid.value
 
     def __call__(self):
