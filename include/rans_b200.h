@@ -109,7 +109,7 @@ int rans_gemv_step_plan(const RansGemvDesc* descs, int n, int R, void* workspace
  * of the first row of that shard inside rank p's FULL output buffer of
  * projection i, this rank included.  The kernel then stores every output row
  * to all npeers buffers (the all-gather of the outputs is fused into the
- * epilogue; npeers <= 8, one node) and fences at system scope; the caller
+ * epilogue; npeers <= 8, one node); the caller
  * runs one cross-GPU barrier after the launch before reading outputs.
  * Replaces the reference's (absent) exchange; no counterpart there. */
 int rans_gemv_step_plan_peers(const RansGemvDesc* descs, const void* const* peer_y, int npeers,

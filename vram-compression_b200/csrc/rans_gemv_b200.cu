@@ -409,13 +409,13 @@ __device__ __forceinline__ void run_pass(const MatDev& d, const uint32_t*, uint1
 
 // Fused output exchange of the row-sharded path: the row goes to every rank's
 // output buffer (plain stores over NVLink; ypeer[] includes this rank's own
-// buffer), followed by a system-scope fence so the stores are performed
-// before the cross-GPU barrier that follows the kernel.
+// buffer).  No fence here: the caller's cross-GPU barrier runs after this
+// kernel in stream order, so these stores happen before its system-scope
+// release, and a fence per row would stall every warp for an NVLink round trip.
 __device__ __forceinline__ void store_peers(const MatDev& d, int row, float s) {
 #pragma unroll
     for (int p = 0; p < kMaxPeers; ++p)
         if (p < d.npeer) d.ypeer[p][row] = s;
-    __threadfence_system();
 }
 
 // Column mode: rows rb*R..rb*R+R-1, column blocks of segment `seg`.
