@@ -485,6 +485,7 @@ __device__ __forceinline__ void process_item(const MatDev& d, int item, const ui
         rowmode_item<R, RowK<R>::value, BF16X>(d, item, tab, stage, lane, bad);
     } else {
         switch (d.kcol) {
+            case 1: colmode_item<R, 1, BF16X>(d, item, tab, stage, lane, bad); break;
             case 2: colmode_item<R, 2, BF16X>(d, item, tab, stage, lane, bad); break;
             case 3: colmode_item<R, 3, BF16X>(d, item, tab, stage, lane, bad); break;
             default: colmode_item<R, 4, BF16X>(d, item, tab, stage, lane, bad); break;
@@ -528,16 +529,103 @@ __global__ void __launch_bounds__(kThreads, RB_MINB) gemv_step_kernel(const Step
     else process_item<R, false>(dl, ch.item0 + warp, tab, stage, lane, bad);
 }
 
-// Decode-only: K consecutive tiles per warp, bf16(code * step) to a dense
-// row-major matrix (the "decompress, then cuBLAS" comparator).
+// One symbol of a staged stream returning kCodeScale*code (no FMA): the
+// decode-to-dense path.  Same sequence as sym_step_ptx.
+__device__ __forceinline__ float sym_code(uint32_t& st, uint32_t& w, uint32_t& pw, uint32_t tb, const uint32_t* tab,
+                                          bool staged, const MatDev& d) {
+#if RB_LAYOUT == 1 && RB_ALIGNTAB
+    if (staged) {
+        float c;
+        asm("{\n\t.reg .pred p;\n\t.reg .b32 e, f, b, hi, a, t;\n\t"
+            "shl.b32 a, %0, 2;\n\t"
+            "and.b32 a, a, 0x3FFC;\n\t"
+            "or.b32 a, a, %4;\n\t"
+            "ld.shared.u32 e, [a];\n\t"
+            "shr.u32 f, e, 20;\n\t"
+            "and.b32 b, e, 4095;\n\t"
+            "shr.u32 hi, %0, 12;\n\t"
+            "mad.lo.u32 %0, f, hi, b;\n\t"
+            "setp.lt.u32 p, %0, 65536;\n\t"
+            "@p prmt.b32 %0, %1, %0, 0x5410;\n\t"
+            "@p add.u32 %2, %2, 2;\n\t"
+            "@p ld.shared.u16 %1, [%2];\n\t"
+            "and.b32 t, e, 0x000FF000;\n\t"
+            "or.b32 t, t, 0x4B000000;\n\t"
+            "sub.f32 %3, t, 0f4B080000;\n\t}"
+            : "+r"(st), "+r"(w), "+r"(pw), "=f"(c)
+            : "r"(tb));
+        return c;
+    }
+#endif
+    const uint32_t e = tab[st & (kProbM - 1)];
+    st = entry_freq(e) * (st >> kScaleBits) + entry_bias(e);
+    if (st < kRansL) {
+        st = __byte_perm(w, st, 0x5410);
+        if (staged) {
+            pw += 2;
+            w = *reinterpret_cast<const uint16_t*>(g_smem + pw);
+        } else {
+            ++pw;
+            w = __ldg(d.words + pw);
+        }
+    }
+    return entry_code(e);
+}
+
+template <int R, int K, bool STAGED>
+__device__ __forceinline__ void decode_store(const MatDev& d, const uint32_t (&pos)[K], int kk,
+                                             __nv_bfloat16* const (&orow)[K], const int (&col0)[K]) {
+    const SmemMap sm = smem_map(0);
+    const bool ptx = STAGED && RB_LAYOUT == 1 && RB_ALIGNTAB;
+    const uint32_t sbase = static_cast<uint32_t>(__cvta_generic_to_shared(g_smem));
+    uint32_t st[K], w[K], p[K];
+#pragma unroll
+    for (int j = 0; j < K; ++j) {
+        p[j] = pos[j];
+        if (STAGED) {
+            st[j] = (static_cast<uint32_t>(*reinterpret_cast<const uint16_t*>(g_smem + p[j])) << 16) |
+                    *reinterpret_cast<const uint16_t*>(g_smem + p[j] + 2);
+            p[j] += 4;
+            w[j] = *reinterpret_cast<const uint16_t*>(g_smem + p[j]);
+            if (ptx) p[j] += sbase;
+        } else {
+            st[j] = (static_cast<uint32_t>(__ldg(d.words + p[j])) << 16) | __ldg(d.words + p[j] + 1);
+            p[j] += 2;
+            w[j] = __ldg(d.words + p[j]);
+        }
+    }
+    const int cols = d.cols;
+    for (int k = 0; k < d.nk; ++k) {
+        float sv[K];
+#pragma unroll
+        for (int j = 0; j < K; ++j) sv[j] = __ldg(d.step + col0[j] + 32 * k) * kInvCodeScale;
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+#pragma unroll
+            for (int j = 0; j < K; ++j) {
+                float c;
+                if (ptx) {
+                    c = sym_code(st[j], w[j], p[j], sm.tab_s, sm.tab, true, d);
+                } else {
+                    // generic pointer bookkeeping of the C++ step uses offsets from g_smem
+                    c = sym_code(st[j], w[j], p[j], sm.tab_s, sm.tab, STAGED, d);
+                }
+                if (j < kk) orow[j][(int64_t)r * cols + 32 * k] = __float2bfloat16(c * sv[j]);
+            }
+        }
+    }
+}
+
+// Decode-only: K consecutive tiles per warp, bf16(code * step) into a dense
+// row-major matrix (the "decompress, then cuBLAS" comparator).  Same staging
+// and symbol step as the fused GEMV; each symbol becomes one 2-byte store,
+// coalesced across the warp (64 B per row segment).
 template <int R, int K>
-__global__ void __launch_bounds__(kThreads) decode_kernel(MatDev d, __nv_bfloat16* __restrict__ out,
-                                                          int64_t ntiles) {
+__global__ void __launch_bounds__(kThreads, RB_MINB) decode_kernel(MatDev d, __nv_bfloat16* __restrict__ out,
+                                                                   int64_t ntiles) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const SmemMap sm = smem_map(warp);
-    uint32_t* tab = sm.tab;
-    uint16_t* stage = sm.stage;
-    load_table(tab, d.table);
+    load_table(sm.tab, d.table);
     __syncthreads();
     const int64_t t0 = ((int64_t)blockIdx.x * kWarps + warp) * K;
     if (t0 >= ntiles) return;
@@ -546,87 +634,71 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(MatDev d, __nv_bfloat1
     const uint32_t w0 = d.offs[s0];
     const uint64_t w1 = span_end(d, s0 + 32ll * kk);
     uint32_t pos[K];
-#pragma unroll
-    for (int j = 0; j < K; ++j) pos[j] = d.offs[s0 + 32 * (j < kk ? j : kk - 1) + lane];
-    const uint16_t* wb = d.words;
-    bool staged = false;
-    if (kStageBytes > 0 && w1 != UINT64_MAX && staged_bytes(d, w0, w1) <= (uint64_t)kStageBytes) {
-        const uint32_t head = stage_span(d, stage, w0, w1, lane);
-#pragma unroll
-        for (int j = 0; j < K; ++j) pos[j] = pos[j] - w0 + head;
-        staged = true;
-    }
-    uint32_t st[K], w[K], p[K];
-    int64_t obase[K];
-    int cbase[K];
+    __nv_bfloat16* orow[K];
+    int col0[K];
 #pragma unroll
     for (int j = 0; j < K; ++j) {
-        const int64_t t = t0 + (j < kk ? j : kk - 1);
+        const int jj = j < kk ? j : kk - 1;
+        pos[j] = d.offs[s0 + 32 * jj + lane];
+        const int64_t t = t0 + jj;
         const int rb = (int)(t / d.ncb), cb = (int)(t % d.ncb);
-        obase[j] = (int64_t)rb * R * d.cols;
-        cbase[j] = cb * d.C + lane;
+        col0[j] = cb * d.C + lane;
+        orow[j] = out + (int64_t)rb * R * d.cols + col0[j];
     }
-    auto body = [&](const uint16_t* base) {
+    if (kStageBytes > 0 && w1 != UINT64_MAX && staged_bytes(d, w0, w1) <= (uint64_t)kStageBytes) {
+        const uint32_t head = stage_span(d, sm.stage, w0, w1, lane);
+        const uint32_t soff = static_cast<uint32_t>(reinterpret_cast<uint8_t*>(sm.stage) - g_smem);
 #pragma unroll
-        for (int j = 0; j < K; ++j) {
-            p[j] = pos[j];
-            st[j] = (static_cast<uint32_t>(base[p[j]]) << 16) | base[p[j] + 1];
-            p[j] += 2;
-            w[j] = base[p[j]];
-        }
-        for (int k = 0; k < d.nk; ++k) {
-            float sv[K];
-#pragma unroll
-            for (int j = 0; j < K; ++j) sv[j] = __ldg(d.step + cbase[j] + 32 * k) * kInvCodeScale;
-#pragma unroll
-            for (int r = 0; r < R; ++r) {
-#pragma unroll
-                for (int j = 0; j < K; ++j) {
-                    const uint32_t e = tab[st[j] & (kProbM - 1)];
-                    st[j] = entry_freq(e) * (st[j] >> kScaleBits) + entry_bias(e);
-                    if (st[j] < kRansL) {
-                        st[j] = __byte_perm(w[j], st[j], 0x5410);
-                        ++p[j];
-                        w[j] = base[p[j]];
-                    }
-                    if (j < kk)
-                        out[obase[j] + (int64_t)r * d.cols + cbase[j] + 32 * k] =
-                            __float2bfloat16(entry_code(e) * sv[j]);
-                }
-            }
-        }
-    };
-    if (staged) body(stage);
-    else body(wb);
+        for (int j = 0; j < K; ++j) pos[j] = soff + 2u * (pos[j] - w0 + head);
+        decode_store<R, K, true>(d, pos, kk, orow, col0);
+    } else {
+        decode_store<R, K, false>(d, pos, kk, orow, col0);
+    }
 }
 
-// Fixed-rate int4 baseline: one warp per row, 16-byte (32-code) loads.
-__global__ void __launch_bounds__(256) int4_gemv_kernel(const uint4* __restrict__ w,
+// Fixed-rate int4 baseline.  A warp owns kInt4Rows consecutive rows: lane l
+// reads the 8-code words g = l, l+32, ... of every row (32-bit loads, 128 B
+// per warp and row, coalesced) and the 8 activations of group g once for all
+// its rows, so x traffic is 1/kInt4Rows of the weight traffic.  A nibble q
+// becomes the float 2^23 + q by one logic op (0x4b000000 | q) and one FADD
+// removes 2^23 + 8.  The kInt4Rows partial sums are transpose-reduced.  The
+// launcher picks kInt4Rows in {8,4,2,1} so that small matrices still get
+// enough warps.
+template <int kInt4Rows>
+__global__ void __launch_bounds__(256) int4_gemv_kernel(const uint32_t* __restrict__ w,
                                                         const float4* __restrict__ x,
                                                         float* __restrict__ y, int rows, int cols) {
     const int lane = threadIdx.x & 31;
-    const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-    if (row >= rows) return;
-    const int nchunk = cols / 32;
-    const uint4* wr = w + (int64_t)row * nchunk;
-    float acc = 0.f;
+    const int row0 = ((blockIdx.x * blockDim.x + threadIdx.x) >> 5) * kInt4Rows;
+    if (row0 >= rows) return;
+    const int ngroup = cols / 8;
+    const uint32_t* wr[kInt4Rows];
+#pragma unroll
+    for (int r = 0; r < kInt4Rows; ++r)
+        wr[r] = w + (int64_t)min(row0 + r, rows - 1) * ngroup;   // rows past the end repeat the last
+    float acc[kInt4Rows];
+#pragma unroll
+    for (int r = 0; r < kInt4Rows; ++r) acc[r] = 0.f;
 #pragma unroll 2
-    for (int j = lane; j < nchunk; j += 32) {
-        const uint4 q = __ldg(wr + j);
-        const uint32_t qs[4] = {q.x, q.y, q.z, q.w};
+    for (int g = lane; g < ngroup; g += 32) {
+        const float4 x0 = __ldg(x + 2 * g);
+        const float4 x1 = __ldg(x + 2 * g + 1);
+        const float xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+        uint32_t q[kInt4Rows];
 #pragma unroll
-        for (int a = 0; a < 4; ++a) {
-            const float4 x0 = __ldg(x + j * 8 + a * 2);
-            const float4 x1 = __ldg(x + j * 8 + a * 2 + 1);
-            const float xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+        for (int r = 0; r < kInt4Rows; ++r) q[r] = __ldg(wr[r] + g);
 #pragma unroll
-            for (int b = 0; b < 8; ++b)
-                acc = fmaf((float)((int)((qs[a] >> (4 * b)) & 15u) - 8), xv[b], acc);
-        }
+        for (int r = 0; r < kInt4Rows; ++r)
+#pragma unroll
+            for (int b = 0; b < 8; ++b) {
+                const float c = __int_as_float(((q[r] >> (4 * b)) & 15u) | 0x4B000000u) - 8388616.0f;
+                acc[r] = fmaf(c, xv[b], acc[r]);
+            }
     }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-    if (lane == 0) y[row] = acc;
+    const float s = reduce_scatter<kInt4Rows>(acc, lane);
+    constexpr int kShift = 5 - Log2<kInt4Rows>::value;
+    const int r = lane >> kShift;
+    if ((lane & ((1 << kShift) - 1)) == 0 && row0 + r < rows) y[row0 + r] = s;
 }
 
 // ------------------------------------------------------------ host side
@@ -663,6 +735,10 @@ static void plan_matrix(MatDev& d, int R, int split_for) {
     else if (d.ncb % 2 == 0) k = 2;
     else k = d.ncb < 4 ? d.ncb : 3;
     if (k < 2) k = 2;
+    // A small matrix that may be split is latency-bound: one tile per warp
+    // gives the most independent warps (the serial chain of one stream is the
+    // floor either way).
+    if (split_for > 0 && (int64_t)d.nrb * d.ncb <= split_for) k = 1;
     d.kcol = k;
     const int passes = (d.ncb + k - 1) / k;
     int nseg = 1;
@@ -762,7 +838,18 @@ extern "C" int rans_gemv_bf16(int R, const void* words, const void* offs, const 
     if (!valid_R(R)) return -1;
     if (!shape_ok(R, rows, cols, C) || step == nullptr) return -2;
     MatDev d = make_desc(words, offs, table, x_bf16, step, y, rows, cols, C, nwords);
-    plan_matrix(d, R, 0);   // y is overwritten: whole row blocks per warp
+    plan_matrix(d, R, 0);   // whole row blocks per warp: y is stored, no atomics
+    if (!d.rowmode && (int64_t)d.nitems * (d.ncb / d.kcol) <= split_target() &&
+        d.ncb > d.kcol) {
+        // Few row blocks with many column blocks (e.g. a 1536 x 8960 down
+        // projection): whole rows give too few warps, so split the column
+        // blocks across warps and accumulate into a zeroed y.
+        plan_matrix(d, R, split_target());
+        if (d.accumulate) {
+            const cudaError_t e = cudaMemsetAsync(y, 0, sizeof(float) * (size_t)rows, stream);
+            if (e != cudaSuccess) return (int)e;
+        }
+    }
     return dispatch_matrix(R, d, true, stream);
 }
 
@@ -800,9 +887,19 @@ extern "C" int launch_int4_gemv(const void* w, const void* x, void* y, int rows,
                                 cudaStream_t stream) {
     if (rows <= 0 || cols <= 0 || cols % 32) return -2;
     const int threads = 256;
-    const int grid = (int)(((int64_t)rows * 32 + threads - 1) / threads);
-    int4_gemv_kernel<<<grid, threads, 0, stream>>>(static_cast<const uint4*>(w), static_cast<const float4*>(x),
-                                                   static_cast<float*>(y), rows, cols);
+    const int64_t want = split_target();
+    const int rw = rows / 8 >= want ? 8 : rows / 4 >= want ? 4 : rows / 2 >= want ? 2 : 1;
+    const int64_t warps = (rows + rw - 1) / rw;
+    const int grid = (int)((warps * 32 + threads - 1) / threads);
+    const uint32_t* wq = static_cast<const uint32_t*>(w);
+    const float4* xv = static_cast<const float4*>(x);
+    float* yv = static_cast<float*>(y);
+    switch (rw) {
+        case 8: int4_gemv_kernel<8><<<grid, threads, 0, stream>>>(wq, xv, yv, rows, cols); break;
+        case 4: int4_gemv_kernel<4><<<grid, threads, 0, stream>>>(wq, xv, yv, rows, cols); break;
+        case 2: int4_gemv_kernel<2><<<grid, threads, 0, stream>>>(wq, xv, yv, rows, cols); break;
+        default: int4_gemv_kernel<1><<<grid, threads, 0, stream>>>(wq, xv, yv, rows, cols); break;
+    }
     return (int)cudaGetLastError();
 }
 
