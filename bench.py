@@ -101,7 +101,8 @@ def make_step(cols, kind, seed):
     return (0.01 * rng.uniform(0.5, 1.5, cols)).astype(np.float32)
 
 
-def build_workload(torch, rb, cfg_name, layers, rank, world, device, log):
+def build_workload(torch, rb, cfg_name, layers, rank, world, device, log, R=None):
+    R = R or R_TILE
     shapes, nlayers, dist, bits, step_kind = CONFIGS[cfg_name]
     nlayers = layers if layers else nlayers
     scale = scale_for_entropy(dist, bits)
@@ -112,7 +113,7 @@ def build_workload(torch, rb, cfg_name, layers, rank, world, device, log):
         for pi, (name, rows, cols) in enumerate(shapes):
             seed = 1000 * li + pi
             codes = make_codes(torch, rows, cols, dist, scale, seed, device)
-            enc = rb.encode(codes, R_TILE, c_tile(cols), nthreads=nthreads)
+            enc = rb.encode(codes, R, c_tile(cols), nthreads=nthreads)
             step = make_step(cols, step_kind, seed + 7)
             if world > 1:
                 enc, row0, nrows = rb.shard_encoding(enc, rank, world)
@@ -257,6 +258,7 @@ def main():
     ap.add_argument("--impl", default="mine", choices=["mine", "reference"])
     ap.add_argument("--config", default="2", choices=sorted(CONFIGS))
     ap.add_argument("--layers", type=int, default=0, help="override layer count (0 = config's)")
+    ap.add_argument("--R", type=int, default=8, choices=[1, 2, 4, 8, 16], help="tile rows of the encoding")
     ap.add_argument("--cpu-budget", type=float, default=12.0, help="seconds of CPU-baseline work")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--exchange", default="fused", choices=["fused", "nccl"],
@@ -270,7 +272,7 @@ def main():
     local = int(os.environ.get("LOCAL_RANK", "0"))
     shapes, nl, dist, bits, _ = CONFIGS[args.config]
     nlayers = args.layers or nl
-    workload = f"qwen2.5-1.5b-step-{dist}{bits}".replace(".", "p")
+    workload = f"qwen2.5-1.5b-step-{dist}{bits}".replace(".", "p") + ("" if args.R == 8 else f"-R{args.R}")
     ncores = len(os.sched_getaffinity(0))
 
     def log(msg):
@@ -321,7 +323,7 @@ def main():
     device = torch.device("cuda", torch.cuda.current_device())
     rb.load()
 
-    mats, meta = build_workload(torch, rb, args.config, nlayers, rank, world, device, log)
+    mats, meta = build_workload(torch, rb, args.config, nlayers, rank, world, device, log, R=args.R)
     # one contiguous activation buffer for the whole step
     xsz = [m.cols for m in mats]
     ysz = [m.rows for m in mats]
@@ -482,7 +484,7 @@ def main():
             "warmup": args.warmup, "ms_per_step": round(t_ms, 4), "higher_is_better": True,
             "scaling": "strong" if world > 1 else "weak", "vs_baseline": None, "dtype": "u16 rANS -> f32",
             "data": "synthetic (seeded random codes, steps and bf16 activations; no checkpoint)",
-            "config": {"workload": workload, "layers": nlayers, "matrices": len(mats), "R": R_TILE,
+            "config": {"workload": workload, "layers": nlayers, "matrices": len(mats), "R": args.R,
                        "C": {str(c): c_tile(c) for c in sorted({c for _, _, c in shapes})},
                        "code_dist": dist, "bits_target": bits, "weights_per_step": weights_step,
                        "compressed_bytes_per_step": alg_bytes * world,

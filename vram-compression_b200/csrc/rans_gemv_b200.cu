@@ -14,10 +14,10 @@
 //     read from shared memory instead of global memory;
 //   * each lane decodes K independent streams (lane l of K tiles) interleaved
 //     symbol by symbol, hiding the table-lookup -> multiply -> compare chain;
-//   * the 16 KB slot table is re-laid in shared memory as
-//       sym | bias << 8 | freq << 20
-//     so freq is one shift, and the code value is built with one byte-permute
-//     as the float 2^23 + sym, minus 2^23 + 128;
+//   * the 16 KB slot table is re-laid in shared memory (16 KB-aligned) as
+//       bias | sym << 12 | freq << 20
+//     so the entry address is one shift + one LOP3, freq one shift, bias one
+//     mask, and 4096*code one LOP3 + FADD (the float 2^23 + 4096*sym);
 //   * fp32 accumulation; the R (or K*R) partial sums per lane are combined with
 //     a transpose-reduce (reduce-scatter) butterfly, R-1 + log2(32/R) shuffles
 //     instead of 5*R, and stored without atomics whenever a warp covers every
@@ -728,13 +728,15 @@ static void plan_matrix(MatDev& d, int R, int split_for) {
         d.nitems = (d.nrb + kr - 1) / kr;
         return;
     }
-    // K that divides ncb (no idle stream slots), preferring more streams per lane
-    int k = 4;
-    if (d.ncb % 4 == 0) k = 4;
-    else if (d.ncb % 3 == 0) k = 3;
-    else if (d.ncb % 2 == 0) k = 2;
-    else k = d.ncb < 4 ? d.ncb : 3;
-    if (k < 2) k = 2;
+    // K that divides ncb (no idle stream slots), preferring more streams per
+    // lane, with at most kPassSymbols symbols per pass so that the pass's words
+    // fit the 8 KB stage up to ~5 bits/symbol.
+    constexpr int64_t kPassSymbols = 12288;
+    const int kmax = (int)std::max<int64_t>(1, std::min<int64_t>(4, kPassSymbols / ((int64_t)R * d.C)));
+    int k = 1;
+    for (int c = kmax; c >= 2; --c)
+        if (d.ncb % c == 0) { k = c; break; }
+    if (k == 1 && kmax >= 2 && d.ncb > 1) k = std::min(kmax, std::min(d.ncb, 3));   // no divisor: accept idle slots
     // A small matrix that may be split is latency-bound: one tile per warp
     // gives the most independent warps (the serial chain of one stream is the
     // floor either way).
