@@ -85,6 +85,8 @@ struct MatDev {
     int npeer;             // > 0: store every output row to all of ypeer[] instead of y
     int pad_[2];
     float* ypeer[kMaxPeers];   // the same rows of every rank's output buffer (peer addresses)
+    float* partials;       // nseg > 1 without accumulate: [nrb][nseg][R] segment sums (workspace)
+    uint32_t* counters;    // [nrb] arrivals per row block, zero between launches (workspace)
 };
 
 struct Chunk {             // one CTA of the step launcher
@@ -124,6 +126,15 @@ __device__ __forceinline__ void cp_async16(uint32_t saddr, const void* gptr) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(saddr), "l"(gptr));
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+
+// Programmatic dependent launch.  A step kernel lets the next kernel of its
+// stream start as soon as all of its CTAs are running, and itself waits for
+// the previous kernel only before it touches anything that kernel may produce
+// or consume (activations, outputs, split counters/partials).  Table loads,
+// offsets and word staging read immutable weights and overlap the previous
+// kernel's tail.  In a kernel launched without the attribute both are no-ops.
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;\n" ::: "memory"); }
 
 // Reference table entry sym | freq<<8 | bias<<20 re-laid for the decoder.
@@ -346,6 +357,7 @@ __device__ __forceinline__ void decode_pass(const uint32_t (&pos)[K], const int 
         if (STAGED && RB_INNER != 0) p[j] += static_cast<uint32_t>(__cvta_generic_to_shared(g_smem));
     }
     const int nk = d.nk;
+    pdl_wait();   // activations may come from the previous kernel of the stream
     float xn[K];
     if (RB_XPREF) load_xs<K, NACC, BF16X>(d, xcol, kk, 0, xn);
     for (int k = 0; k < nk; ++k) {
@@ -436,10 +448,32 @@ __device__ void colmode_item(const MatDev& d, int item, const uint32_t* tab, uin
         for (int j = 0; j < K; ++j) xcol[j] = (cb0 + (j < kk ? j : 0)) * d.C + lane;
         run_pass<R, K, 1, BF16X>(d, tab, stage, (int64_t)rb * d.ncb + cb0, kk, xcol, acc, bad, lane);
     }
-    const float s = reduce_scatter<R>(acc[0], lane) * kInvCodeScale;
+    float s = reduce_scatter<R>(acc[0], lane) * kInvCodeScale;
     constexpr int kShift = 5 - Log2<R>::value;
-    if ((lane & ((1 << kShift) - 1)) == 0) {
-        const int row = rb * R + (lane >> kShift);
+    const bool owner = (lane & ((1 << kShift) - 1)) == 0;
+    const int r = lane >> kShift;
+    if (d.nseg > 1 && d.partials != nullptr) {
+        // Row block split over nseg warps: publish this segment's R sums, and
+        // let the last warp to finish add all segments in segment order
+        // (deterministic) and store y.  The counter is reset for the next launch.
+        if (owner) d.partials[((int64_t)rb * d.nseg + seg) * R + r] = s;
+        __threadfence();
+        __syncwarp();
+        uint32_t prev = 0;
+        if (lane == 0) prev = atomicAdd(d.counters + rb, 1u);
+        prev = __shfl_sync(0xffffffffu, prev, 0);
+        if (prev != (uint32_t)d.nseg - 1) return;
+        if (lane == 0) d.counters[rb] = 0u;
+        __threadfence();
+        if (owner) {
+            const volatile float* part = d.partials + (int64_t)rb * d.nseg * R + r;
+            float t = 0.f;
+            for (int g = 0; g < d.nseg; ++g) t += part[(int64_t)g * R];
+            s = t;
+        }
+    }
+    if (owner) {
+        const int row = rb * R + r;
         if (d.accumulate) atomicAdd(d.y + row, s);
         else if (d.npeer > 0) store_peers(d, row, s);
         else d.y[row] = s;
@@ -517,6 +551,7 @@ __global__ void __launch_bounds__(kThreads, RB_MINB) gemv_step_kernel(const Step
     const Chunk ch = chunks[blockIdx.x];
     const MatDev& d = descs[ch.desc];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    pdl_launch_dependents();
     const SmemMap sm = smem_map(warp);
     uint32_t* tab = sm.tab;
     uint16_t* stage = sm.stage;
@@ -923,11 +958,51 @@ static int64_t count_chunks(const RansGemvDesc* descs, int n, int R, std::vector
     return nchunks;
 }
 
+// Work plan of a step launch: decomposition of every matrix plus the
+// workspace layout [header][MatDev x n][Chunk x nchunks][counters][partials].
+// A launch with few whole-row items (a small phase of a decoder step: q/k/v,
+// o, down) leaves most SMs idle and is bound by a few long serial chains, so
+// its column-mode matrices are split to one tile per warp; the segments of a
+// row block meet in `partials` and the last-arriving warp stores y.
+struct StepLayout {
+    std::vector<MatDev> mats;
+    int64_t nchunks = 0;
+    size_t counters_off = 0, partials_off = 0, bytes = 0;
+};
+
+static size_t align16(size_t v) { return (v + 15) & ~size_t(15); }
+
+static int layout_step(const RansGemvDesc* descs, int n, int R, StepLayout& L) {
+    L.mats.clear();
+    if (count_chunks(descs, n, R, &L.mats) < 0) return -2;
+    int64_t items = 0;
+    for (const MatDev& d : L.mats) items += d.nitems;
+    const bool split = items * 2 < split_target();
+    int64_t ncounters = 0, npartials = 0;
+    L.nchunks = 0;
+    for (MatDev& d : L.mats) {
+        if (split && !d.rowmode && d.ncb > 1) {
+            d.kcol = 1;
+            d.nseg = d.ncb;
+            d.cbs = 1;
+            d.nitems = d.nrb * d.ncb;
+            d.accumulate = 0;
+            ncounters += d.nrb;
+            npartials += (int64_t)d.nrb * d.nseg * R;
+        }
+        L.nchunks += (d.nitems + kWarps - 1) / kWarps;
+    }
+    L.counters_off = align16(step_bytes(n, L.nchunks));
+    L.partials_off = align16(L.counters_off + sizeof(uint32_t) * (size_t)ncounters);
+    L.bytes = L.partials_off + sizeof(float) * (size_t)npartials;
+    return 0;
+}
+
 extern "C" int64_t rans_gemv_step_workspace_bytes(const RansGemvDesc* descs, int n, int R) {
     if (!valid_R(R) || n <= 0) return -1;
-    const int64_t nchunks = count_chunks(descs, n, R, nullptr);
-    if (nchunks < 0) return -2;
-    return (int64_t)step_bytes(n, nchunks);
+    StepLayout L;
+    if (layout_step(descs, n, R, L) != 0) return -2;
+    return (int64_t)L.bytes;
 }
 
 static int plan_step(const RansGemvDesc* descs, const void* const* peer_y, int npeers, int n, int R,
@@ -949,17 +1024,29 @@ static int plan_step(const RansGemvDesc* descs, const void* const* peer_y, int n
                      void* workspace, size_t workspace_bytes, int* grid_out, cudaStream_t stream) {
     if (!valid_R(R)) return -1;
     if (n <= 0) return -2;
-    std::vector<MatDev> mats;
-    const int64_t nchunks = count_chunks(descs, n, R, &mats);
-    if (nchunks < 0) return -2;
+    StepLayout L;
+    if (layout_step(descs, n, R, L) != 0) return -2;
+    std::vector<MatDev>& mats = L.mats;
+    const int64_t nchunks = L.nchunks;
     for (int i = 0; i < n && peer_y != nullptr; ++i) {
-        if (mats[i].accumulate) return -2;   // split rows cannot be exchanged by stores
+        if (mats[i].accumulate) return -2;   // atomically accumulated rows cannot be exchanged by stores
         mats[i].npeer = npeers;
         for (int p = 0; p < npeers; ++p)
             mats[i].ypeer[p] = static_cast<float*>(const_cast<void*>(peer_y[(size_t)i * npeers + p]));
     }
-    if (step_bytes(n, nchunks) > workspace_bytes) return -3;
-    std::vector<uint8_t> host(step_bytes(n, nchunks));
+    if (L.bytes > workspace_bytes) return -3;
+    // counters (zeroed here, reset by the kernel after each use) and partials
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    int64_t coff = 0, poff = 0;
+    for (MatDev& d : mats) {
+        if (d.nseg > 1 && !d.accumulate) {
+            d.counters = reinterpret_cast<uint32_t*>(ws + L.counters_off) + coff;
+            d.partials = reinterpret_cast<float*>(ws + L.partials_off) + poff;
+            coff += d.nrb;
+            poff += (int64_t)d.nrb * d.nseg * R;
+        }
+    }
+    std::vector<uint8_t> host(L.partials_off, 0);
     StepHeader* h = reinterpret_cast<StepHeader*>(host.data());
     h->ndesc = n;
     h->nchunks = (int)nchunks;
@@ -997,7 +1084,21 @@ template <int R>
 static int launch_step_t(const void* ws, int nchunks, cudaStream_t stream) {
     static unsigned long long done = 0;
     set_smem_attr((const void*)gemv_step_kernel<R>, &done);
-    gemv_step_kernel<R><<<nchunks, kThreads, kSmemBytes, stream>>>(static_cast<const StepHeader*>(ws));
+    // programmatic dependent launch: may start while the previous kernel of the
+    // stream drains; the kernel waits for it before touching activations/outputs
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(nchunks);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = kSmemBytes;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const StepHeader* h = static_cast<const StepHeader*>(ws);
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, gemv_step_kernel<R>, h);
+    if (e != cudaSuccess) return (int)e;
     return (int)cudaGetLastError();
 }
 
