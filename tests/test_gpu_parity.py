@@ -181,3 +181,30 @@ def test_reference_kernel_agrees(torch, rb):
     a = mine.gemv(xt).cpu().numpy()
     b = theirs.gemv(xt).cpu().numpy()
     assert orc.rel_l2(a, b) < 1e-5
+
+
+def test_chained_steps_read_previous_output(torch, rb):
+    """Step kernels start early (programmatic dependent launch) but must read
+    activations only after the previous kernel finished: launch B's input is
+    launch A's output (fp32, already step-scaled), repeated back to back."""
+    rng = np.random.default_rng(11)
+    codes_a = orc.synth_codes(1024, 1536, 3.25, "laplace", seed=21)   # y_a has 1024 rows
+    codes_b = orc.synth_codes(512, 1024, 4.25, "gauss", seed=22)      # consumes 1024 columns
+    step_a = (0.01 * rng.uniform(0.5, 1.5, 1536)).astype(np.float32)
+    ma = rb.RansMatrix(rb.encode(codes_a, 8, 512), torch.from_numpy(step_a))
+    mb = rb.RansMatrix(rb.encode(codes_b, 8, 512), torch.ones(1024))
+    xa = torch.from_numpy(rng.standard_normal(1536).astype(np.float32)).bfloat16().cuda()
+    ya = torch.empty(1024, device="cuda")
+    yb = torch.empty(512, device="cuda")
+    sa = rb.RansStep([ma], [xa], [ya])
+    sb = rb.RansStep([mb], [ya], [yb], prescaled_x=True)   # B reads ya as fp32, already scaled
+    ya_ref = orc.gemv(codes_a, step_a.astype(np.float64), xa.float().cpu().numpy().astype(np.float64))
+    for _ in range(20):
+        ya.fill_(float("nan"))
+        yb.fill_(float("nan"))
+        sa()
+        sb()
+    torch.cuda.synchronize()
+    _check_y(ya.cpu().numpy(), ya_ref)
+    yb_ref = orc.gemv(codes_b, np.ones(1024), ya.cpu().numpy().astype(np.float64))
+    _check_y(yb.cpu().numpy(), yb_ref)

@@ -325,10 +325,13 @@ class RansStep:
     The plan is built once; __call__ is a single asynchronous launch.
     """
 
-    def __init__(self, mats, xs, ys, lib=None, peers=None):
+    def __init__(self, mats, xs, ys, lib=None, peers=None, prescaled_x=False):
         """peers: optional, per matrix the device addresses (valid on this GPU)
         of the matching rows in every rank's output buffer; the kernel then
-        writes each output row to all of them (fused all-gather)."""
+        writes each output row to all of them (fused all-gather).
+        prescaled_x: xs are fp32 activations already multiplied by the step
+        (the reference's convention) instead of bf16 with the step applied
+        in-kernel."""
         torch = _torch()
         self.lib = _lib(lib)
         if not mats:
@@ -338,7 +341,7 @@ class RansStep:
             raise ValueError("all matrices of a step must share R")
         self.R = R
         self.mats, self.xs, self.ys = list(mats), list(xs), list(ys)
-        arr = (RansGemvDesc * len(mats))(*[m.desc(x, y) for m, x, y in zip(mats, xs, ys)])
+        arr = (RansGemvDesc * len(mats))(*[m.desc(x, y, step=not prescaled_x) for m, x, y in zip(mats, xs, ys)])
         self._descs = arr
         nbytes = self.lib.rans_gemv_step_workspace_bytes(ctypes.addressof(arr), len(mats), R)
         if nbytes < 0:
