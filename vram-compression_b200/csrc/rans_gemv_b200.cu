@@ -49,6 +49,12 @@ constexpr int kPadWords = 8;
 #ifndef RB_MINB
 #define RB_MINB 2        // 2 CTAs/SM: lets ptxas use up to 128 registers (no rematerialisation)
 #endif
+#ifndef RB_PDL
+#define RB_PDL 1         // programmatic dependent launch of the step kernel
+#endif
+#ifndef RB_PREFETCH
+#define RB_PREFETCH 0    // each CTA warms L2 for the chunk one wave ahead (measured: no gain)
+#endif
 #ifndef RB_LAYOUT
 #define RB_LAYOUT 1      // shared-memory table entry: 0 = sym|bias<<8|freq<<20, 1 = bias|sym<<12|freq<<20
 #endif
@@ -94,7 +100,10 @@ struct Chunk {             // one CTA of the step launcher
 };
 
 struct StepHeader {
-    int ndesc, nchunks, R, pad_;
+    int ndesc, nchunks, R;
+    int ahead;             // L2-prefetch distance in chunks (co-resident CTAs), 0 = off
+    int64_t spans_off;     // byte offset of uint2 spans[nchunks] (word range per chunk)
+    int64_t pad_;
 };
 
 // The CTA's dynamic shared memory: the 16 KB slot table and one stage per
@@ -543,6 +552,58 @@ __global__ void __launch_bounds__(kThreads, RB_MINB) gemv_matrix_kernel(MatDev d
     process_item<R, BF16X>(d, item, tab, stage, lane, bad);
 }
 
+// Tiles [t_begin, t_end) of a work item (consecutive in stream order).
+__device__ __forceinline__ void item_tiles(const MatDev& d, int R, int item, int64_t& t_begin, int64_t& t_end) {
+    if (d.rowmode) {
+        const int kr = R >= 8 ? 32 / R : 4;
+        t_begin = (int64_t)item * kr;
+        t_end = min((int64_t)d.nrb, t_begin + kr);
+    } else {
+        const int rb = item / d.nseg, seg = item - rb * d.nseg;
+        t_begin = (int64_t)rb * d.ncb + seg * d.cbs;
+        t_end = (int64_t)rb * d.ncb + min(d.ncb, seg * d.cbs + d.cbs);
+    }
+}
+
+// Plan-time: the contiguous word range [x, y) of every chunk.
+__global__ void fill_spans_kernel(const StepHeader* __restrict__ hdr, int R) {
+    const int c = blockIdx.x * blockDim.x + threadIdx.x;
+    if (c >= hdr->nchunks) return;
+    const MatDev* descs = reinterpret_cast<const MatDev*>(hdr + 1);
+    const Chunk* chunks = reinterpret_cast<const Chunk*>(descs + hdr->ndesc);
+    uint2* spans = reinterpret_cast<uint2*>(const_cast<uint8_t*>(reinterpret_cast<const uint8_t*>(hdr) + hdr->spans_off));
+    const Chunk ch = chunks[c];
+    const MatDev& d = descs[ch.desc];
+    int64_t t0, t1, u0, u1;
+    item_tiles(d, R, ch.item0, t0, t1);
+    item_tiles(d, R, ch.item0 + ch.nitems - 1, u0, u1);
+    const uint32_t w0 = d.offs[t0 * 32];
+    const uint64_t w1 = span_end(d, u1 * 32);
+    spans[c] = make_uint2(w0, w1 == UINT64_MAX ? w0 : static_cast<uint32_t>(w1));
+}
+
+// TMA bulk prefetch of [p, p + bytes) into L2, 16-byte aligned outward (each
+// 16-byte block touched overlaps the range, so no page outside it is touched).
+__device__ __forceinline__ void prefetch_l2(const void* p, uint64_t bytes) {
+    uintptr_t a = reinterpret_cast<uintptr_t>(p) & ~uintptr_t(15);
+    const uintptr_t e = (reinterpret_cast<uintptr_t>(p) + bytes + 15) & ~uintptr_t(15);
+    for (; a < e; a += 65536) {
+        const uint32_t n = static_cast<uint32_t>(e - a < 65536 ? e - a : 65536);
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;\n" ::"l"(a), "r"(n) : "memory");
+    }
+}
+
+// Warm L2 for the chunk that starts about one wave after this CTA: its words,
+// offsets and table, while this CTA loads its own.
+__device__ __forceinline__ void prefetch_next_chunk(const StepHeader* hdr, const MatDev* descs, const Chunk* chunks) {
+    const int nb = blockIdx.x + hdr->ahead;
+    if (hdr->ahead <= 0 || nb >= hdr->nchunks) return;
+    const uint2 sp = reinterpret_cast<const uint2*>(reinterpret_cast<const uint8_t*>(hdr) + hdr->spans_off)[nb];
+    const MatDev& dn = descs[chunks[nb].desc];
+    if (sp.y > sp.x) prefetch_l2(dn.words + sp.x, 2ull * (sp.y - sp.x));
+    prefetch_l2(dn.table, kTableBytes);
+}
+
 // Every projection of a decoder step: CTA b processes chunk b (one matrix).
 template <int R>
 __global__ void __launch_bounds__(kThreads, RB_MINB) gemv_step_kernel(const StepHeader* __restrict__ hdr) {
@@ -551,7 +612,8 @@ __global__ void __launch_bounds__(kThreads, RB_MINB) gemv_step_kernel(const Step
     const Chunk ch = chunks[blockIdx.x];
     const MatDev& d = descs[ch.desc];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    pdl_launch_dependents();
+    if (RB_PDL) pdl_launch_dependents();
+    if (RB_PREFETCH && threadIdx.x == kThreads - 1) prefetch_next_chunk(hdr, descs, chunks);
     const SmemMap sm = smem_map(warp);
     uint32_t* tab = sm.tab;
     uint16_t* stage = sm.stage;
@@ -967,7 +1029,7 @@ static int64_t count_chunks(const RansGemvDesc* descs, int n, int R, std::vector
 struct StepLayout {
     std::vector<MatDev> mats;
     int64_t nchunks = 0;
-    size_t counters_off = 0, partials_off = 0, bytes = 0;
+    size_t counters_off = 0, partials_off = 0, spans_off = 0, bytes = 0;
 };
 
 static size_t align16(size_t v) { return (v + 15) & ~size_t(15); }
@@ -994,7 +1056,8 @@ static int layout_step(const RansGemvDesc* descs, int n, int R, StepLayout& L) {
     }
     L.counters_off = align16(step_bytes(n, L.nchunks));
     L.partials_off = align16(L.counters_off + sizeof(uint32_t) * (size_t)ncounters);
-    L.bytes = L.partials_off + sizeof(float) * (size_t)npartials;
+    L.spans_off = align16(L.partials_off + sizeof(float) * (size_t)npartials);
+    L.bytes = L.spans_off + sizeof(uint2) * (size_t)L.nchunks;
     return 0;
 }
 
@@ -1007,6 +1070,30 @@ extern "C" int64_t rans_gemv_step_workspace_bytes(const RansGemvDesc* descs, int
 
 static int plan_step(const RansGemvDesc* descs, const void* const* peer_y, int npeers, int n, int R,
                      void* workspace, size_t workspace_bytes, int* grid_out, cudaStream_t stream);
+
+// CTAs of the step kernel resident at once on the whole GPU (the L2-prefetch
+// distance: chunk b + resident starts roughly when chunk b's CTA is running).
+template <int R>
+static int resident_ctas_t() {
+    static unsigned long long done = 0;
+    set_smem_attr((const void*)gemv_step_kernel<R>, &done);
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, gemv_step_kernel<R>, kThreads, kSmemBytes) !=
+        cudaSuccess)
+        return 0;
+    return per_sm * sm_count();
+}
+
+static int resident_ctas(int R) {
+    switch (R) {
+        case 1: return resident_ctas_t<1>();
+        case 2: return resident_ctas_t<2>();
+        case 4: return resident_ctas_t<4>();
+        case 8: return resident_ctas_t<8>();
+        case 16: return resident_ctas_t<16>();
+        default: return 0;
+    }
+}
 
 extern "C" int rans_gemv_step_plan(const RansGemvDesc* descs, int n, int R, void* workspace,
                                    size_t workspace_bytes, int* grid_out, cudaStream_t stream) {
@@ -1051,6 +1138,8 @@ static int plan_step(const RansGemvDesc* descs, const void* const* peer_y, int n
     h->ndesc = n;
     h->nchunks = (int)nchunks;
     h->R = R;
+    h->ahead = resident_ctas(R);
+    h->spans_off = (int64_t)L.spans_off;
     MatDev* md = reinterpret_cast<MatDev*>(h + 1);
     Chunk* ch = reinterpret_cast<Chunk*>(md + n);
     int64_t c = 0;
@@ -1075,6 +1164,11 @@ static int plan_step(const RansGemvDesc* descs, const void* const* peer_y, int n
     if (grid_out) *grid_out = (int)nchunks;
     cudaError_t e = cudaMemcpyAsync(workspace, host.data(), host.size(), cudaMemcpyHostToDevice, stream);
     if (e != cudaSuccess) return (int)e;
+    // word span of every chunk (needs the device offsets), for the L2 prefetch
+    fill_spans_kernel<<<(unsigned)((nchunks + 255) / 256), 256, 0, stream>>>(
+        static_cast<const StepHeader*>(workspace), R);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return (int)e;
     // the pageable source must stay valid until the copy has been staged
     e = cudaStreamSynchronize(stream);
     return (int)e;
@@ -1095,7 +1189,7 @@ static int launch_step_t(const void* ws, int nchunks, cudaStream_t stream) {
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = RB_PDL ? 1 : 0;
     const StepHeader* h = static_cast<const StepHeader*>(ws);
     const cudaError_t e = cudaLaunchKernelEx(&cfg, gemv_step_kernel<R>, h);
     if (e != cudaSuccess) return (int)e;
@@ -1165,6 +1259,8 @@ extern "C" int rans_gemv_step_noalloc(const RansGemvDesc* descs, int n, int R, c
     h->ndesc = n;
     h->nchunks = (int)nchunks;
     h->R = R;
+    h->ahead = 0;         // no span table here: no L2 prefetch
+    h->spans_off = 0;
     h->pad_ = 0;
     MatDev* md = reinterpret_cast<MatDev*>(h + 1);
     Chunk* ch = reinterpret_cast<Chunk*>(md + n);
