@@ -440,6 +440,9 @@ __device__ __forceinline__ void store_peers(const MatDev& d, int row, float s) {
 }
 
 // Column mode: rows rb*R..rb*R+R-1, column blocks of segment `seg`.
+template <int R>
+__device__ __forceinline__ void colmode_epilogue(const MatDev& d, int rb, int seg, float s, int lane);
+
 template <int R, int K, bool BF16X>
 __device__ void colmode_item(const MatDev& d, int item, const uint32_t* tab, uint16_t* stage,
                              int lane, int& bad) {
@@ -457,7 +460,13 @@ __device__ void colmode_item(const MatDev& d, int item, const uint32_t* tab, uin
         for (int j = 0; j < K; ++j) xcol[j] = (cb0 + (j < kk ? j : 0)) * d.C + lane;
         run_pass<R, K, 1, BF16X>(d, tab, stage, (int64_t)rb * d.ncb + cb0, kk, xcol, acc, bad, lane);
     }
-    float s = reduce_scatter<R>(acc[0], lane) * kInvCodeScale;
+    colmode_epilogue<R>(d, rb, seg, reduce_scatter<R>(acc[0], lane) * kInvCodeScale, lane);
+}
+
+// Output of one column-mode item: lane l holds the full 32-lane sum s of row
+// rb*R + (l >> (5 - log2 R)).
+template <int R>
+__device__ __forceinline__ void colmode_epilogue(const MatDev& d, int rb, int seg, float s, int lane) {
     constexpr int kShift = 5 - Log2<R>::value;
     const bool owner = (lane & ((1 << kShift) - 1)) == 0;
     const int r = lane >> kShift;
