@@ -555,10 +555,11 @@ __global__ void __launch_bounds__(kThreads, RB_MINB) gemv_matrix_kernel(MatDev d
     uint16_t* stage = sm.stage;
     load_table(tab, d.table);
     __syncthreads();
-    const int item = blockIdx.x * kWarps + warp;
-    if (item >= d.nitems) return;
+    // grid-stride over items: the grid holds only as many CTAs as fit on the
+    // GPU at once, so a large matrix has no half-empty last wave
     int bad = 0;
-    process_item<R, BF16X>(d, item, tab, stage, lane, bad);
+    for (int item = blockIdx.x * kWarps + warp; item < d.nitems; item += gridDim.x * kWarps)
+        process_item<R, BF16X>(d, item, tab, stage, lane, bad);
 }
 
 // Tiles [t_begin, t_end) of a work item (consecutive in stream order).
@@ -727,14 +728,8 @@ __device__ __forceinline__ void decode_store(const MatDev& d, const uint32_t (&p
 // and symbol step as the fused GEMV; each symbol becomes one 2-byte store,
 // coalesced across the warp (64 B per row segment).
 template <int R, int K>
-__global__ void __launch_bounds__(kThreads, RB_MINB) decode_kernel(MatDev d, __nv_bfloat16* __restrict__ out,
-                                                                   int64_t ntiles) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const SmemMap sm = smem_map(warp);
-    load_table(sm.tab, d.table);
-    __syncthreads();
-    const int64_t t0 = ((int64_t)blockIdx.x * kWarps + warp) * K;
-    if (t0 >= ntiles) return;
+__device__ __forceinline__ void decode_tiles(const MatDev& d, const SmemMap& sm, __nv_bfloat16* __restrict__ out,
+                                             int64_t ntiles, int64_t t0, int lane) {
     const int kk = ntiles - t0 < K ? (int)(ntiles - t0) : K;
     const int64_t s0 = t0 * 32;
     const uint32_t w0 = d.offs[s0];
@@ -759,6 +754,21 @@ __global__ void __launch_bounds__(kThreads, RB_MINB) decode_kernel(MatDev d, __n
         decode_store<R, K, true>(d, pos, kk, orow, col0);
     } else {
         decode_store<R, K, false>(d, pos, kk, orow, col0);
+    }
+}
+
+// Grid-stride over groups of K tiles; the grid holds only resident CTAs.
+template <int R, int K>
+__global__ void __launch_bounds__(kThreads, RB_MINB) decode_kernel(MatDev d, __nv_bfloat16* __restrict__ out,
+                                                                   int64_t ntiles) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const SmemMap sm = smem_map(warp);
+    load_table(sm.tab, d.table);
+    __syncthreads();
+    const int64_t stride = (int64_t)gridDim.x * kWarps * K;
+    for (int64_t t0 = ((int64_t)blockIdx.x * kWarps + warp) * K; t0 < ntiles; t0 += stride) {
+        decode_tiles<R, K>(d, sm, out, ntiles, t0, lane);
+        __syncwarp();   // every lane is done with this span before the stage is refilled
     }
 }
 
@@ -818,8 +828,9 @@ static int sm_count() {
     return n;
 }
 
-// Fills the work decomposition of d.  `split_for` > 0 asks for at least that
-// many items (column blocks then split across warps, accumulating into y).
+// Fills the work decomposition of d.  `split_for` > 0 is the number of warps
+// resident at once and allows column blocks to be split across warps
+// (accumulating into y) where that shortens the launch.
 static void plan_matrix(MatDev& d, int R, int split_for) {
     d.ncb = d.cols / d.C;
     d.nrb = d.rows / R;
@@ -849,10 +860,20 @@ static void plan_matrix(MatDev& d, int R, int split_for) {
     if (split_for > 0 && (int64_t)d.nrb * d.ncb <= split_for) k = 1;
     d.kcol = k;
     const int passes = (d.ncb + k - 1) / k;
+    // Segments per row block (equal: a divisor of passes), chosen for the
+    // shortest makespan when split_for warps run at once: waves of items times
+    // passes per item, plus a small per-item cost (setup, reduction, atomics)
+    // of 1/20 pass.  Few row blocks -> many segments so every warp has work;
+    // many row blocks -> segments still shrink the last, partly idle wave.
     int nseg = 1;
     if (split_for > 0) {
-        while (nseg < passes && (int64_t)d.nrb * nseg < split_for) ++nseg;
-        while (passes % nseg) ++nseg;   // equal segments
+        int64_t best = INT64_MAX;
+        for (int s = 1; s <= passes; ++s) {
+            if (passes % s) continue;
+            const int64_t waves = ((int64_t)d.nrb * s + split_for - 1) / split_for;
+            const int64_t cost = waves * (20ll * (passes / s) + 1);
+            if (cost < best) { best = cost; nseg = s; }
+        }
     }
     d.nseg = nseg;
     d.cbs = (passes / nseg) * k;
@@ -873,19 +894,34 @@ static bool set_smem_attr(const void* fn, unsigned long long* done_mask) {
     return true;
 }
 
+// CTAs of `fn` (kThreads threads, kSmemBytes shared) resident at once on the
+// current device; cached per device in `cache` (0 = not yet asked).
+static int resident_blocks(const void* fn, int* cache) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 1;
+    int* slot = &cache[dev & 63];
+    int v = __atomic_load_n(slot, __ATOMIC_ACQUIRE);
+    if (v > 0) return v;
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kThreads, kSmemBytes) != cudaSuccess ||
+        per_sm < 1)
+        per_sm = 1;
+    v = per_sm * sm_count();
+    __atomic_store_n(slot, v, __ATOMIC_RELEASE);
+    return v;
+}
+
 template <int R>
 static int launch_matrix(const MatDev& d, bool bf16x, cudaStream_t stream) {
-    const int grid = (d.nitems + kWarps - 1) / kWarps;
+    int grid = (d.nitems + kWarps - 1) / kWarps;
     if (grid == 0) return 0;
-    if (bf16x) {
-        static unsigned long long done = 0;
-        set_smem_attr((const void*)gemv_matrix_kernel<R, true>, &done);
-        gemv_matrix_kernel<R, true><<<grid, kThreads, kSmemBytes, stream>>>(d);
-    } else {
-        static unsigned long long done = 0;
-        set_smem_attr((const void*)gemv_matrix_kernel<R, false>, &done);
-        gemv_matrix_kernel<R, false><<<grid, kThreads, kSmemBytes, stream>>>(d);
-    }
+    const void* fn = bf16x ? (const void*)gemv_matrix_kernel<R, true> : (const void*)gemv_matrix_kernel<R, false>;
+    static unsigned long long done[2] = {0, 0};
+    static int resident[2][64] = {};
+    set_smem_attr(fn, &done[bf16x ? 1 : 0]);
+    grid = std::min(grid, resident_blocks(fn, resident[bf16x ? 1 : 0]));
+    if (bf16x) gemv_matrix_kernel<R, true><<<grid, kThreads, kSmemBytes, stream>>>(d);
+    else gemv_matrix_kernel<R, false><<<grid, kThreads, kSmemBytes, stream>>>(d);
     return (int)cudaGetLastError();
 }
 
@@ -947,11 +983,15 @@ extern "C" int rans_gemv_bf16(int R, const void* words, const void* offs, const 
     if (!shape_ok(R, rows, cols, C) || step == nullptr) return -2;
     MatDev d = make_desc(words, offs, table, x_bf16, step, y, rows, cols, C, nwords);
     plan_matrix(d, R, 0);   // whole row blocks per warp: y is stored, no atomics
-    if (!d.rowmode && (int64_t)d.nitems * (d.ncb / d.kcol) <= split_target() &&
-        d.ncb > d.kcol) {
+    // (row mode has kcol = 0 and is never split)
+    const bool few = !d.rowmode && (int64_t)d.nitems * (d.ncb / d.kcol) <= split_target();
+    const bool many = !d.rowmode && d.nitems > split_target();
+    if ((few || many) && d.ncb > d.kcol) {
         // Few row blocks with many column blocks (e.g. a 1536 x 8960 down
-        // projection): whole rows give too few warps, so split the column
-        // blocks across warps and accumulate into a zeroed y.
+        // projection): whole rows give too few warps; more row blocks than
+        // one wave of warps: whole rows leave the last wave partly idle.
+        // Either way split the column blocks across warps and accumulate
+        // into a zeroed y.
         plan_matrix(d, R, split_target());
         if (d.accumulate) {
             const cudaError_t e = cudaMemsetAsync(y, 0, sizeof(float) * (size_t)rows, stream);
@@ -965,9 +1005,12 @@ template <int R, int K>
 static int launch_decode_t(const MatDev& d, void* out, cudaStream_t stream) {
     const int64_t ntiles = (int64_t)d.nrb * d.ncb;
     const int64_t warps = (ntiles + K - 1) / K;
-    const int grid = (int)((warps + kWarps - 1) / kWarps);
+    int64_t grid = (warps + kWarps - 1) / kWarps;
+    if (grid == 0) return 0;
     static unsigned long long done = 0;
+    static int resident[64] = {};
     set_smem_attr((const void*)decode_kernel<R, K>, &done);
+    grid = std::min<int64_t>(grid, resident_blocks((const void*)decode_kernel<R, K>, resident));
     decode_kernel<R, K><<<grid, kThreads, kSmemBytes, stream>>>(d, static_cast<__nv_bfloat16*>(out), ntiles);
     return (int)cudaGetLastError();
 }
