@@ -29,6 +29,8 @@
 #include <mutex>
 #include <vector>
 
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
@@ -82,6 +84,8 @@ struct MatDev {
     const float* step;     // NULL: x is fp32 pre-scaled; else x is bf16
     float* y;
     int64_t nwords;        // incl. pad, or -1
+    int64_t wlimit;        // nwords < 0: words readable from `words` on (to the end of its
+                           // device allocation), 0 = unknown
     int rows, cols, C, ncb, nrb, nk;
     int rowmode;           // 1: ncb == 1, item = KROW row blocks
     int kcol;              // column-mode streams per lane (2..4)
@@ -89,7 +93,8 @@ struct MatDev {
     int nitems;
     int accumulate;        // 1: atomicAdd into y (split rows), 0: store
     int npeer;             // > 0: store every output row to all of ypeer[] instead of y
-    int pad_[2];
+    int tail_words;        // most words one stream can hold: 2 state words + one per symbol
+    int pad_;
     float* ypeer[kMaxPeers];   // the same rows of every rank's output buffer (peer addresses)
     float* partials;       // nseg > 1 without accumulate: [nrb][nseg][R] segment sums (workspace)
     uint32_t* counters;    // [nrb] arrivals per row block, zero between launches (workspace)
@@ -245,6 +250,14 @@ __device__ __forceinline__ uint64_t span_end(const MatDev& d, int64_t s_end) {
     const int64_t nstreams = (int64_t)d.nrb * d.ncb * 32;
     if (s_end < nstreams) return d.offs[s_end];
     if (d.nwords >= 0) return (uint64_t)(d.nwords - kPadWords);
+    if (d.wlimit > 0) {
+        // Length unknown (the reference entry points pass none): the final
+        // stream ends within tail_words of its start (a symbol takes at most
+        // one renormalisation word) and within the words' device allocation,
+        // so staging up to the nearer bound copies every word it holds.
+        const uint64_t e = (uint64_t)d.offs[nstreams - 1] + (uint64_t)d.tail_words;
+        return e < (uint64_t)d.wlimit ? e : (uint64_t)d.wlimit;
+    }
     return UINT64_MAX;
 }
 
@@ -556,10 +569,13 @@ __global__ void __launch_bounds__(kThreads, RB_MINB) gemv_matrix_kernel(MatDev d
     load_table(tab, d.table);
     __syncthreads();
     // grid-stride over items: the grid holds only as many CTAs as fit on the
-    // GPU at once, so a large matrix has no half-empty last wave
+    // GPU at once, so a large matrix has no half-empty last wave.  Items are
+    // taken last-first: without a known buffer length (the reference entry
+    // points pass none) the item holding the final stream cannot be staged
+    // and is the slowest, so it starts in the first wave.
     int bad = 0;
-    for (int item = blockIdx.x * kWarps + warp; item < d.nitems; item += gridDim.x * kWarps)
-        process_item<R, BF16X>(d, item, tab, stage, lane, bad);
+    for (int i = blockIdx.x * kWarps + warp; i < d.nitems; i += gridDim.x * kWarps)
+        process_item<R, BF16X>(d, d.nitems - 1 - i, tab, stage, lane, bad);
 }
 
 // Tiles [t_begin, t_end) of a work item (consecutive in stream order).
@@ -757,7 +773,9 @@ __device__ __forceinline__ void decode_tiles(const MatDev& d, const SmemMap& sm,
     }
 }
 
-// Grid-stride over groups of K tiles; the grid holds only resident CTAs.
+// Grid-stride over groups of K tiles, last group first (it holds the final
+// stream, unstaged when the buffer length is unknown); the grid holds only
+// resident CTAs.
 template <int R, int K>
 __global__ void __launch_bounds__(kThreads, RB_MINB) decode_kernel(MatDev d, __nv_bfloat16* __restrict__ out,
                                                                    int64_t ntiles) {
@@ -765,9 +783,9 @@ __global__ void __launch_bounds__(kThreads, RB_MINB) decode_kernel(MatDev d, __n
     const SmemMap sm = smem_map(warp);
     load_table(sm.tab, d.table);
     __syncthreads();
-    const int64_t stride = (int64_t)gridDim.x * kWarps * K;
-    for (int64_t t0 = ((int64_t)blockIdx.x * kWarps + warp) * K; t0 < ntiles; t0 += stride) {
-        decode_tiles<R, K>(d, sm, out, ntiles, t0, lane);
+    const int64_t ngroups = (ntiles + K - 1) / K;
+    for (int64_t g = (int64_t)blockIdx.x * kWarps + warp; g < ngroups; g += (int64_t)gridDim.x * kWarps) {
+        decode_tiles<R, K>(d, sm, out, ntiles, (ngroups - 1 - g) * K, lane);
         __syncwarp();   // every lane is done with this span before the stage is refilled
     }
 }
@@ -835,6 +853,7 @@ static void plan_matrix(MatDev& d, int R, int split_for) {
     d.ncb = d.cols / d.C;
     d.nrb = d.rows / R;
     d.nk = d.C / 32;
+    d.tail_words = 2 + R * d.nk;
     d.rowmode = d.ncb == 1 ? 1 : 0;
     d.accumulate = 0;
     if (d.rowmode) {
@@ -940,6 +959,28 @@ static bool shape_ok(int R, int rows, int cols, int C) {
     return rows > 0 && cols > 0 && C > 0 && C % 32 == 0 && cols % C == 0 && rows % R == 0;
 }
 
+// Words readable from `words` to the end of the mapped device memory region
+// holding it (cuMemGetAddressRange, reached through the runtime's driver entry
+// point so there is no link to libcuda), 0 when the driver does not know the
+// pointer.
+static int64_t readable_words(const void* words) {
+    static const PFN_cuMemGetAddressRange_v3020 fn = [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+        if (cudaGetDriverEntryPointByVersion("cuMemGetAddressRange", &p, 12000, cudaEnableDefault, &q) !=
+                cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            return static_cast<PFN_cuMemGetAddressRange_v3020>(nullptr);
+        return reinterpret_cast<PFN_cuMemGetAddressRange_v3020>(p);
+    }();
+    if (fn == nullptr || words == nullptr) return 0;
+    CUdeviceptr base = 0;
+    size_t size = 0;
+    const CUdeviceptr w = reinterpret_cast<CUdeviceptr>(words);
+    if (fn(&base, &size, w) != CUDA_SUCCESS || w < base || w >= base + size) return 0;
+    return static_cast<int64_t>((base + size - w) / 2);
+}
+
 static MatDev make_desc(const void* words, const void* offs, const void* table, const void* x,
                         const void* step, void* y, int rows, int cols, int C, int64_t nwords) {
     MatDev d;
@@ -951,6 +992,7 @@ static MatDev make_desc(const void* words, const void* offs, const void* table, 
     d.step = static_cast<const float*>(step);
     d.y = static_cast<float*>(y);
     d.nwords = nwords;
+    d.wlimit = nwords < 0 ? readable_words(words) : 0;
     d.rows = rows;
     d.cols = cols;
     d.C = C;
@@ -983,19 +1025,24 @@ extern "C" int rans_gemv_bf16(int R, const void* words, const void* offs, const 
     if (!shape_ok(R, rows, cols, C) || step == nullptr) return -2;
     MatDev d = make_desc(words, offs, table, x_bf16, step, y, rows, cols, C, nwords);
     plan_matrix(d, R, 0);   // whole row blocks per warp: y is stored, no atomics
-    // (row mode has kcol = 0 and is never split)
-    const bool few = !d.rowmode && (int64_t)d.nitems * (d.ncb / d.kcol) <= split_target();
-    const bool many = !d.rowmode && d.nitems > split_target();
-    if ((few || many) && d.ncb > d.kcol) {
-        // Few row blocks with many column blocks (e.g. a 1536 x 8960 down
-        // projection): whole rows give too few warps; more row blocks than
-        // one wave of warps: whole rows leave the last wave partly idle.
-        // Either way split the column blocks across warps and accumulate
-        // into a zeroed y.
-        plan_matrix(d, R, split_target());
-        if (d.accumulate) {
-            const cudaError_t e = cudaMemsetAsync(y, 0, sizeof(float) * (size_t)rows, stream);
-            if (e != cudaSuccess) return (int)e;
+    if (!d.rowmode) {   // (row mode has kcol = 0 and is never split)
+        // Splitting the column blocks of a row block across warps (and
+        // accumulating into a zeroed y) pays when whole rows give too few
+        // warps (e.g. a 1536 x 8960 down projection), or when it shortens the
+        // launch by 10% or more: makespan = waves of items x column blocks
+        // per item, with split_target() warps per wave.
+        const int64_t W = split_target();
+        MatDev s = d;
+        plan_matrix(s, R, (int)W);
+        const bool few = (int64_t)d.nitems * (d.ncb / d.kcol) <= W;
+        const int64_t span_whole = (d.nitems + W - 1) / W * d.cbs;
+        const int64_t span_split = (s.nitems + W - 1) / W * s.cbs;
+        if (few || span_split * 10 < span_whole * 9) {
+            d = s;
+            if (d.accumulate) {
+                const cudaError_t e = cudaMemsetAsync(y, 0, sizeof(float) * (size_t)rows, stream);
+                if (e != cudaSuccess) return (int)e;
+            }
         }
     }
     return dispatch_matrix(R, d, true, stream);
@@ -1024,6 +1071,7 @@ extern "C" int launch_rans_decode(int R, const void* words, const void* offs, co
     d.ncb = cols / C;
     d.nrb = rows / R;
     d.nk = C / 32;
+    d.tail_words = 2 + R * d.nk;
     switch (R) {
         case 1: return launch_decode_t<1, 2>(d, out, stream);
         case 2: return launch_decode_t<2, 2>(d, out, stream);
