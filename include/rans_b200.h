@@ -160,6 +160,26 @@ int rans_encode_host(const int8_t* codes, int rows, int cols, int R, int C,
                      const uint32_t* table, uint16_t* words, int64_t words_cap,
                      uint32_t* offs, int64_t* nwords_out, int nthreads);
 
+/* ------------------------------------------------------------ escape codes
+ * Codes outside [-128, 127] (the reference's encoder rejects them,
+ * kernel/rans.py:65-66; "escape codes" are listed as future work in its
+ * README) are stored in the stream as an in-range fill code and kept in a
+ * sparse list of n (row, col) pairs, int32 each.  No counterpart in the
+ * reference.  Both launch one thread per escape on `stream` and return 0, a
+ * CUDA error, or -2 for bad arguments. */
+
+/* y[rows[i]] += delta[i] * x'[cols[i]] (atomicAdd), delta = code - fill as
+ * fp32.  x' = x (fp32, pre-scaled, the launch_rans_gemv convention) when
+ * step is NULL, else bf16 x times fp32 step (the rans_gemv_bf16 convention).
+ * Run after the GEMV that wrote y. */
+int rans_escape_gemv(const void* rows, const void* cols, const void* delta, int n,
+                     const void* x, const void* step, void* y, cudaStream_t stream);
+
+/* out[rows[i] * ncols + cols[i]] = bf16(codes[i] * step[cols[i]]), codes
+ * int32.  Run after launch_rans_decode wrote out. */
+int rans_escape_decode(const void* rows, const void* cols, const void* codes, int n,
+                       const void* step, void* out, int ncols, cudaStream_t stream);
+
 /* ABI version (RANS_B200_ABI_VERSION). */
 int rans_b200_abi_version(void);
 

@@ -866,8 +866,8 @@ static void plan_matrix(MatDev& d, int R, int split_for) {
     }
     // K that divides ncb (no idle stream slots), preferring more streams per
     // lane, with at most kPassSymbols symbols per pass so that the pass's words
-    // fit the 8 KB stage up to ~5 bits/symbol.
-    constexpr int64_t kPassSymbols = 12288;
+    // fit the stage up to ~5 bits/symbol.
+    constexpr int64_t kPassSymbols = kStageBytes > 0 ? kStageBytes * 3 / 2 : 12288;
     const int kmax = (int)std::max<int64_t>(1, std::min<int64_t>(4, kPassSymbols / ((int64_t)R * d.C)));
     int k = 1;
     for (int c = kmax; c >= 2; --c)

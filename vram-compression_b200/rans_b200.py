@@ -66,6 +66,10 @@ def _bind(lib):
     lib.rans_encode_bound.restype = _i64
     lib.rans_encode_host.argtypes = [_vp, _i32, _i32, _i32, _i32, _vp, _vp, _i64, _vp, _vp, _i32]
     lib.rans_encode_host.restype = _i32
+    lib.rans_escape_gemv.argtypes = [_vp, _vp, _vp, _i32, _vp, _vp, _vp, _vp]
+    lib.rans_escape_gemv.restype = _i32
+    lib.rans_escape_decode.argtypes = [_vp, _vp, _vp, _i32, _vp, _vp, _i32, _vp]
+    lib.rans_escape_decode.restype = _i32
     lib.rans_b200_abi_version.argtypes = []
     lib.rans_b200_abi_version.restype = _i32
     return lib
