@@ -66,7 +66,9 @@ def test_container_to_layer(torch, tmp_path):
     loaded, _ = rm.load_matrices(path)
     a, b = rm.RansLinear(m), rm.RansLinear(loaded["w"])
     x = torch.randn(1024).bfloat16().cuda()
-    assert torch.equal(a.gemv(x), b.gemv(x))
+    # same kernels on the same bytes; only the order of fp32 atomic adds
+    # (split column blocks, escapes) may differ between the two calls
+    assert orc.rel_l2(a.gemv(x).cpu().numpy(), b.gemv(x).cpu().numpy()) < 1e-6
     assert torch.equal(a.weight_bf16(), b.weight_bf16())
 
 

@@ -846,6 +846,19 @@ static int sm_count() {
     return n;
 }
 
+// Most symbols one staged pass should hold: 85% of the stage at the matrix's
+// mean size per symbol (state words included) when the buffer length is
+// known, else a bound for up to ~5.3 bits/symbol.  A pass whose span still
+// does not fit is decoded from global memory (same results, slower).
+static int64_t pass_symbols(const MatDev& d) {
+    if (kStageBytes <= 0) return 12288;
+    if (d.nwords > 0 && d.rows > 0 && d.cols > 0) {
+        const double bytes_per_symbol = 2.0 * (double)d.nwords / ((double)d.rows * (double)d.cols);
+        return std::max<int64_t>(1, (int64_t)(0.85 * kStageBytes / bytes_per_symbol));
+    }
+    return (int64_t)kStageBytes * 3 / 2;
+}
+
 // Fills the work decomposition of d.  `split_for` > 0 is the number of warps
 // resident at once and allows column blocks to be split across warps
 // (accumulating into y) where that shortens the launch.
@@ -865,10 +878,9 @@ static void plan_matrix(MatDev& d, int R, int split_for) {
         return;
     }
     // K that divides ncb (no idle stream slots), preferring more streams per
-    // lane, with at most kPassSymbols symbols per pass so that the pass's words
-    // fit the stage up to ~5 bits/symbol.
-    constexpr int64_t kPassSymbols = kStageBytes > 0 ? kStageBytes * 3 / 2 : 12288;
-    const int kmax = (int)std::max<int64_t>(1, std::min<int64_t>(4, kPassSymbols / ((int64_t)R * d.C)));
+    // lane, with at most pass_symbols(d) symbols per pass so that the pass's
+    // words fit the stage.
+    const int kmax = (int)std::max<int64_t>(1, std::min<int64_t>(4, pass_symbols(d) / ((int64_t)R * d.C)));
     int k = 1;
     for (int c = kmax; c >= 2; --c)
         if (d.ncb % c == 0) { k = c; break; }
@@ -1142,18 +1154,55 @@ static int layout_step(const RansGemvDesc* descs, int n, int R, StepLayout& L) {
     const bool split = items * 2 < split_target();
     int64_t ncounters = 0, npartials = 0;
     L.nchunks = 0;
-    for (MatDev& d : L.mats) {
-        if (split && !d.rowmode && d.ncb > 1) {
-            d.kcol = 1;
-            d.nseg = d.ncb;
-            d.cbs = 1;
-            d.nitems = d.nrb * d.ncb;
-            d.accumulate = 0;
-            ncounters += d.nrb;
-            npartials += (int64_t)d.nrb * d.nseg * R;
+    if (split) {
+        // Split column-mode matrices into segments of T consecutive tiles,
+        // decoded as T interleaved streams in one pass.  Start from T = 1 (the
+        // most warps) and, while the launch has more items than warps resident
+        // at once, coarsen the matrix with the most items to its next T that
+        // divides ncb (T <= 4): a second, mostly idle wave would cost a whole
+        // serial chain, more T costs only interleaving.
+        const int64_t W = split_target();
+        std::vector<int> T(L.mats.size(), 0);
+        int64_t total = 0;
+        for (size_t i = 0; i < L.mats.size(); ++i) {
+            const MatDev& d = L.mats[i];
+            if (!d.rowmode && d.ncb > 1) T[i] = 1;
+            total += T[i] ? (int64_t)d.nrb * d.ncb : d.nitems;
         }
-        L.nchunks += (d.nitems + kWarps - 1) / kWarps;
+        auto next_t = [&](size_t i) {
+            const MatDev& d = L.mats[i];
+            for (int t = T[i] + 1; t <= 4 && (int64_t)t * R * d.C <= pass_symbols(d); ++t)
+                if (d.ncb % t == 0) return t;
+            return 0;
+        };
+        while (total > W) {
+            size_t best = SIZE_MAX;
+            int64_t best_items = 0;
+            for (size_t i = 0; i < L.mats.size(); ++i) {
+                if (!T[i] || !next_t(i)) continue;
+                const int64_t it = (int64_t)L.mats[i].nrb * (L.mats[i].ncb / T[i]);
+                if (it > best_items) { best_items = it; best = i; }
+            }
+            if (best == SIZE_MAX) break;
+            const int t = next_t(best);
+            total -= best_items - (int64_t)L.mats[best].nrb * (L.mats[best].ncb / t);
+            T[best] = t;
+        }
+        for (size_t i = 0; i < L.mats.size(); ++i) {
+            if (!T[i]) continue;
+            MatDev& d = L.mats[i];
+            d.kcol = T[i];
+            d.nseg = d.ncb / T[i];
+            d.cbs = T[i];
+            d.nitems = d.nrb * d.nseg;
+            d.accumulate = 0;
+            if (d.nseg > 1) {
+                ncounters += d.nrb;
+                npartials += (int64_t)d.nrb * d.nseg * R;
+            }
+        }
     }
+    for (MatDev& d : L.mats) L.nchunks += (d.nitems + kWarps - 1) / kWarps;
     L.counters_off = align16(step_bytes(n, L.nchunks));
     L.partials_off = align16(L.counters_off + sizeof(uint32_t) * (size_t)ncounters);
     L.spans_off = align16(L.partials_off + sizeof(float) * (size_t)npartials);

@@ -242,9 +242,12 @@ class RansMatrix:
         self.rows, self.cols = enc["shape"]
         dev = device if device is not None else torch.device("cuda", torch.cuda.current_device())
         self.device = dev
-        self.words = torch.from_numpy(np.ascontiguousarray(enc["words"]).view(np.int16)).to(dev)
-        self.offs = torch.from_numpy(np.ascontiguousarray(enc["offs"]).view(np.int32)).to(dev)
-        self.table = torch.from_numpy(np.ascontiguousarray(enc["table"]).view(np.int32)).to(dev)
+        # (np.require copies read-only inputs such as memory-mapped files: torch
+        # wraps only writable arrays)
+        host = lambda a, t: torch.from_numpy(np.require(a, requirements=["C", "W"]).view(t))
+        self.words = host(enc["words"], np.int16).to(dev)
+        self.offs = host(enc["offs"], np.int32).to(dev)
+        self.table = host(enc["table"], np.int32).to(dev)
         step = step if hasattr(step, "float") else torch.from_numpy(np.asarray(step, np.float32))
         self.step = step.float().to(dev).contiguous()
         self.nwords = int(self.words.numel())
