@@ -471,7 +471,7 @@ def main():
         lb.record(stream)
         torch.cuda.synchronize()
         lms = la.elapsed_time(lb) / nrep
-        layered = {"us_per_token_step": round(lms * 1e3, 2), "launches_per_step": len(phase_steps),
+        layered = {"us_per_token_step": round(lms * 1e3, 2), "launches_per_step": sum(p.kernels for p in phase_steps),
                    "how": "per layer 4 dependent phases ({q,k,v}, o, {gate,up}, down), one launch each, "
                           "one CUDA graph per step"}
         del g
@@ -555,7 +555,7 @@ def main():
                        "compressed_bytes_per_step": alg_bytes * world,
                        "l2": "inputs (compressed weights) larger than the 126 MB L2; no flush",
                        "parallelism": f"row-shard x{world}" if world > 1 else "single GPU",
-                       "launches_per_step": 1},
+                       "launches_per_step": step.kernels},
             "us_per_token_step": round(t_ms * 1e3, 2),
             "layered": layered,
             "compressed_gbs": round(compressed_gbs_step, 2),
@@ -563,7 +563,7 @@ def main():
                          "frac": round(achieved / peak, 4), "traffic": traffic, "peak_kind": peak_kind,
                          "kernel": "gemv_step_kernel", "kernel_ms": round(k_ms, 4)},
             "tsymbols_per_s": round(weights_step / (t_ms * 1e-3) / 1e12, 4),
-            "gpu_launches": args.steps,
+            "gpu_launches": args.steps * step.kernels,
             "clocks": clocks,
             "e2e": {"value": round(e2e_val, 2), "unit": "GB/s", "ms_per_step": round(e2e_ms, 4),
                     "h2d_bytes_per_step": int(x_all.numel() * 2), "d2h_bytes_per_step": int(y_all.numel() * 4)},

@@ -69,8 +69,8 @@ int launch_int4_gemv(const void* w, const void* x, void* y, int rows, int cols,
 /* Same GEMV with the step folded inside the kernel: x is bf16[cols], step is
  * fp32[cols]; y (fp32[rows]) is overwritten (no zero-fill needed).
  * nwords = total length of `words` in words (including the 8 pad words), or
- * -1 when unknown (the stream holding the matrix's last words is then read
- * straight from global memory instead of being staged).
+ * -1 when unknown (the final pass is then staged up to the end of the device
+ * memory region holding `words`, as for the drop-in entry points).
  * Additive variant of kernel/rans.py:140-152 (RansMatrix.gemv), whose host
  * multiply x.float()*step (rans.py:141) moves into the kernel. */
 int rans_gemv_bf16(int R, const void* words, const void* offs, const void* table,
@@ -116,12 +116,16 @@ int rans_gemv_step_plan_peers(const RansGemvDesc* descs, const void* const* peer
                               int n, int R, void* workspace, size_t workspace_bytes,
                               int* grid_out, cudaStream_t stream);
 
-/* Run every projection of a decoder step from ONE grid (one kernel launch,
- * capturable in a CUDA graph).  Each CTA loads the slot table of its matrix
- * and its warps decode whole row blocks, so y is stored without atomics.
- * No counterpart in the reference: its harness launches one kernel per
- * matrix (kernel/bench.py:104-107, kernel/rans.py:147-151). */
+/* Run every projection of a decoder step from ONE grid (capturable in a
+ * CUDA graph).  Each CTA loads the slot table of its matrix and its warps
+ * decode whole row blocks, so y is stored without atomics.  A plan of two or
+ * more waves of work with bf16 activations first runs one small kernel that
+ * writes x*step (fp32) into the workspace; rans_gemv_step_kernels tells how
+ * many kernels a launch of a planned workspace runs (1 or 2).  No counterpart
+ * in the reference: its harness launches one kernel per matrix
+ * (kernel/bench.py:104-107, kernel/rans.py:147-151). */
 int rans_gemv_step_launch(int R, const void* workspace, int grid, cudaStream_t stream);
+int rans_gemv_step_kernels(const void* workspace);
 
 /* The same decoder step for callers that cannot allocate device memory when
  * they run it: a framework whose caching allocator owns the whole pool (a

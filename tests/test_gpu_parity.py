@@ -208,3 +208,35 @@ def test_chained_steps_read_previous_output(torch, rb):
     _check_y(ya.cpu().numpy(), ya_ref)
     yb_ref = orc.gemv(codes_b, np.ones(1024), ya.cpu().numpy().astype(np.float64))
     _check_y(yb.cpu().numpy(), yb_ref)
+
+
+def test_throughput_step_prescale_reads_fresh_activations(torch, rb):
+    """A throughput plan (enough whole-row items, not split) first turns bf16
+    x into x*step in its workspace with a small kernel, then decodes.  The
+    activations are rewritten by an ordinary kernel before every launch; each
+    launch must see the new values (the prescale waits for the previous
+    kernel of the stream), and the result must match the float64 oracle."""
+    mats, xs, ys, codes_l, steps = [], [], [], [], []
+    encs = {}
+    for seed in (31, 32):
+        codes = orc.synth_codes(8960, 1536, 4.25, "gauss", seed=seed)
+        encs[seed] = (codes, rb.encode(codes, 8, 512))
+    for i in range(6):   # 6 x 1120 whole-row items: a multi-wave launch, so the plan prescales
+        seed = 31 + i % 2
+        codes, enc = encs[seed]
+        step = (0.01 * np.random.default_rng(100 + i).uniform(0.5, 1.5, 1536)).astype(np.float32)
+        mats.append(rb.RansMatrix(enc, torch.from_numpy(step)))
+        xs.append(torch.empty(1536, device="cuda", dtype=torch.bfloat16))
+        ys.append(torch.empty(8960, device="cuda"))
+        codes_l.append(codes)
+        steps.append(step)
+    st = rb.RansStep(mats, xs, ys)
+    g = torch.Generator(device="cuda").manual_seed(5)
+    for it in range(6):
+        srcs = [torch.randn(1536, device="cuda", generator=g) for _ in xs]
+        for x, src in zip(xs, srcs):
+            x.copy_(src.bfloat16())
+        st()
+    torch.cuda.synchronize()
+    for x, y, codes, step in zip(xs, ys, codes_l, steps):
+        _check_y(y.cpu().numpy(), _y64(codes, step, x.float().cpu().numpy()))

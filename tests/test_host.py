@@ -146,3 +146,26 @@ print("planned ok")
     env = dict(os.environ, CUDA_VISIBLE_DEVICES="")
     r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=300)
     assert r.returncode == 0 and "planned ok" in r.stdout, (r.returncode, r.stdout[-1000:], r.stderr[-2000:])
+
+
+def _descs(n, rows, cols, C, bf16_x, nwords=1 << 20):
+    arr = (rb.RansGemvDesc * n)()
+    for i in range(n):
+        # pointers are never dereferenced by the workspace query
+        arr[i] = rb.RansGemvDesc(256, 256, 256, 256, 256 if bf16_x else None, 256, nwords, rows, cols, C, 0)
+    return arr
+
+
+def test_step_workspace_layout_without_gpu(lib):
+    """Host-side step planning: a multi-wave launch with bf16 activations gets
+    a prescaled fp32 copy of every activation vector in its workspace; a
+    short (split) launch and fp32 activations do not."""
+    big_bf16 = lib.rans_gemv_step_workspace_bytes(_descs(6, 8960, 1536, 512, True), 6, 8)
+    big_f32 = lib.rans_gemv_step_workspace_bytes(_descs(6, 8960, 1536, 512, False), 6, 8)
+    assert big_bf16 > 0 and big_f32 > 0
+    assert big_bf16 - big_f32 >= 6 * 1536 * 4          # x' copies + their job table
+    small_bf16 = lib.rans_gemv_step_workspace_bytes(_descs(1, 256, 1536, 512, True), 1, 8)
+    small_f32 = lib.rans_gemv_step_workspace_bytes(_descs(1, 256, 1536, 512, False), 1, 8)
+    assert small_bf16 == small_f32
+    assert lib.rans_gemv_step_workspace_bytes(_descs(1, 12, 1536, 512, True), 1, 8) == -2   # rows % R
+    assert lib.rans_gemv_step_workspace_bytes(_descs(1, 256, 1536, 512, True), 1, 3) == -1  # bad R

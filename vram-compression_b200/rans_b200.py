@@ -60,6 +60,8 @@ def _bind(lib):
     lib.rans_gemv_step_plan_peers.restype = _i32
     lib.rans_gemv_step_launch.argtypes = [_i32, _vp, _i32, _vp]
     lib.rans_gemv_step_launch.restype = _i32
+    lib.rans_gemv_step_kernels.argtypes = [_vp]
+    lib.rans_gemv_step_kernels.restype = _i32
     lib.rans_build_table_host.argtypes = [_vp, _i64, _vp, _vp, _vp, _i32]
     lib.rans_build_table_host.restype = _i32
     lib.rans_encode_bound.argtypes = [_i32] * 4
@@ -329,7 +331,8 @@ class RansStep:
 
     `mats` are RansMatrix objects sharing one R; xs are their activations
     (bf16, step folded in-kernel) and ys their fp32 outputs (overwritten).
-    The plan is built once; __call__ is a single asynchronous launch.
+    The plan is built once; __call__ is one asynchronous launch (of
+    `self.kernels` kernels: a large bf16-activation plan adds a prescale).
     """
 
     def __init__(self, mats, xs, ys, lib=None, peers=None, prescaled_x=False):
@@ -370,6 +373,7 @@ class RansStep:
                                                     ctypes.byref(grid), _stream(torch))
             _check(rc, "rans_gemv_step_plan_peers")
         self.grid = grid.value
+        self.kernels = int(self.lib.rans_gemv_step_kernels(self.workspace.data_ptr()))   # per launch
 
     def __call__(self):
         torch = _torch()
