@@ -364,21 +364,9 @@ def main():
     if world > 1 and args.exchange == "fused":
         # every rank holds the FULL outputs of every projection in symmetric
         # memory; the kernel stores its shard rows into all ranks' copies
-        import torch.distributed as dist_
-        import torch.distributed._symmetric_memory as symm_mem
-        full = [m["rows"] for m in meta]
-        F = np.concatenate([[0], np.cumsum(full)[:-1]]).astype(np.int64)
-        y_all = symm_mem.empty(int(sum(full)), dtype=torch.float32, device=device)
-        y_all.zero_()
-        try:
-            hdl = symm_mem.rendezvous(y_all, dist_.group.WORLD)
-        except Exception:
-            symm_mem.enable_symm_mem_for_group(dist_.group.WORLD.group_name)
-            hdl = symm_mem.rendezvous(y_all, dist_.group.WORLD)
-        ptrs = [int(p) for p in hdl.buffer_ptrs]
-        ys = [y_all[int(F[i]) + m["row0"]: int(F[i]) + m["row0"] + m["nrows"]] for i, m in enumerate(meta)]
-        peers = [[ptrs[p] + 4 * (int(F[i]) + m["row0"]) for p in range(world)] for i, m in enumerate(meta)]
-        step = rb.RansStep(mats, xs, ys, peers=peers)
+        import rans_dist
+        sharded = rans_dist.ShardedStep(mats, [m["rows"] for m in meta], xs, exchange="fused", timeout_ms=60000)
+        step, hdl, y_all, F = sharded.step, sharded.hdl, sharded.y_full, sharded.layout.F
 
         def gather():
             hdl.barrier(channel=0, timeout_ms=60000)

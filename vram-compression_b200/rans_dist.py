@@ -1,0 +1,175 @@
+"""Row-sharded multi-GPU decoder step (one process per GPU, torch.distributed).
+
+Every projection's row blocks are split into one contiguous range per rank
+(`shard_rows`, the same split as rans_b200.shard_encoding); because the streams
+of consecutive row blocks are consecutive, a rank's shard is a slice of the
+encoding, not a re-encoding.  Each rank decodes its rows of every projection
+in one step launch, and the outputs are exchanged in one of two ways:
+
+  fused  the step kernel's epilogue stores every output row into the FULL
+         output buffer of every rank (torch symmetric memory, NVLink stores),
+         then one cross-GPU barrier (bounded: it raises after `timeout_ms`);
+  nccl   the step writes local rows, then one all-gather per call
+         (`gather_rows`, any backend: NCCL on GPUs, gloo on CPU).
+
+The reference has no multi-GPU path; this is the exchange step its survey
+describes (one all-gather of y per projection), fused into the kernel.
+"""
+from __future__ import annotations
+
+import numpy as np
+
+import rans_b200 as rb
+
+
+def shard_rows(rows: int, R: int, rank: int, world: int):
+    """(first row, row count) of `rank`'s contiguous row-block range."""
+    if rows % R:
+        raise ValueError("rows must be a multiple of R")
+    if not 0 <= rank < world:
+        raise ValueError("rank out of range")
+    nrb = rows // R
+    rb0, rb1 = nrb * rank // world, nrb * (rank + 1) // world
+    return rb0 * R, (rb1 - rb0) * R
+
+
+class ShardLayout:
+    """Where every projection's shard rows live in the concatenated full
+    outputs: projection i occupies [F[i], F[i] + rows[i]) of the full buffer
+    and rank r's rows of it start at F[i] + row0[i][r]."""
+
+    def __init__(self, rows, R: int, world: int):
+        self.rows = [int(r) for r in rows]
+        self.R, self.world = R, world
+        self.F = np.concatenate([[0], np.cumsum(self.rows)[:-1]]).astype(np.int64)
+        self.total = int(sum(self.rows))
+        self.row0 = [[shard_rows(r, R, k, world)[0] for k in range(world)] for r in self.rows]
+        self.nrows = [[shard_rows(r, R, k, world)[1] for k in range(world)] for r in self.rows]
+
+    def local_slices(self, rank: int):
+        """(start, stop) of rank's rows of every projection in the full buffer."""
+        return [(int(self.F[i]) + self.row0[i][rank], int(self.F[i]) + self.row0[i][rank] + self.nrows[i][rank])
+                for i in range(len(self.rows))]
+
+    def peer_addresses(self, buffer_ptrs, rank: int, elem_bytes: int = 4):
+        """Per projection, the address of rank's first shard row inside every
+        rank's full buffer (buffer_ptrs[p] = base address of rank p's buffer as
+        seen from this GPU)."""
+        if len(buffer_ptrs) != self.world:
+            raise ValueError("one buffer pointer per rank")
+        return [[int(buffer_ptrs[p]) + elem_bytes * (int(self.F[i]) + self.row0[i][rank])
+                 for p in range(self.world)] for i in range(len(self.rows))]
+
+
+def gather_rows(local, counts, group=None):
+    """All-gather row shards of different lengths (rank order) into the full
+    vector: pad to the longest shard, all_gather, trim.  Any backend."""
+    import torch
+    import torch.distributed as dist
+    world = dist.get_world_size(group)
+    if len(counts) != world:
+        raise ValueError("one row count per rank")
+    mx = max(int(c) for c in counts)
+    buf = torch.zeros(mx, dtype=local.dtype, device=local.device)
+    buf[: local.numel()] = local
+    parts = [torch.empty_like(buf) for _ in range(world)]
+    dist.all_gather(parts, buf, group=group)
+    return torch.cat([p[: int(c)] for p, c in zip(parts, counts)])
+
+
+def regroup_rank_major(gathered, layout: ShardLayout):
+    """Rank-major gathered rows (rank 0's rows of projections 0..n-1, then
+    rank 1's, ...) -> the full output of every projection."""
+    import torch
+    out = [torch.empty(r, dtype=gathered.dtype, device=gathered.device) for r in layout.rows]
+    pos = 0
+    for r in range(layout.world):
+        for i in range(len(out)):
+            n, a = layout.nrows[i][r], layout.row0[i][r]
+            out[i][a:a + n].copy_(gathered[pos:pos + n])
+            pos += n
+    if pos != gathered.numel():
+        raise ValueError("gathered rows do not match the layout")
+    return out
+
+
+class ShardedStep:
+    """This rank's share of a decoder step whose projections are row-sharded
+    over the ranks of the default process group.
+
+    mats: this rank's row shards (RansMatrix, in projection order, e.g. from
+    rans_b200.shard_encoding); full_rows: every projection's full row count;
+    xs: this rank's activations (bf16, all columns).  After a call, `full[i]`
+    is projection i's complete output on this rank (fused exchange), or
+    `full_outputs()` assembles it (nccl exchange, one all-gather per call).
+    """
+
+    def __init__(self, mats, full_rows, xs, exchange: str = "fused", timeout_ms: int = 60000, lib=None):
+        import torch
+        import torch.distributed as dist
+        if exchange not in ("fused", "nccl"):
+            raise ValueError("exchange must be 'fused' or 'nccl'")
+        if len(mats) != len(full_rows) or len(xs) != len(mats):
+            raise ValueError("one shard, one full row count and one activation per projection")
+        self.rank, self.world = dist.get_rank(), dist.get_world_size()
+        R = mats[0].R
+        self.layout = ShardLayout(full_rows, R, self.world)
+        for i, m in enumerate(mats):
+            if m.rows != self.layout.nrows[i][self.rank]:
+                raise ValueError(f"projection {i}: shard has {m.rows} rows, "
+                                 f"rank {self.rank} owns {self.layout.nrows[i][self.rank]}")
+        dev = mats[0].device
+        self.exchange, self.timeout_ms = exchange, timeout_ms
+        self.mats = list(mats)
+        sl = self.layout.local_slices(self.rank)
+        self.hdl = None
+        if exchange == "fused":
+            import torch.distributed._symmetric_memory as symm_mem
+            self.y_full = symm_mem.empty(self.layout.total, dtype=torch.float32, device=dev)
+            self.y_full.zero_()
+            try:
+                self.hdl = symm_mem.rendezvous(self.y_full, dist.group.WORLD)
+            except Exception:
+                symm_mem.enable_symm_mem_for_group(dist.group.WORLD.group_name)
+                self.hdl = symm_mem.rendezvous(self.y_full, dist.group.WORLD)
+            peers = self.layout.peer_addresses([int(p) for p in self.hdl.buffer_ptrs], self.rank)
+            ys = [self.y_full[a:b] for a, b in sl]
+            self.step = rb.RansStep(self.mats, xs, ys, lib=lib, peers=peers)
+            self.full = [self.y_full[int(self.layout.F[i]):int(self.layout.F[i]) + self.layout.rows[i]]
+                         for i in range(len(mats))]
+        else:
+            n_local = sum(b - a for a, b in sl)
+            self.y_local = torch.zeros(n_local, device=dev)
+            offs = np.concatenate([[0], np.cumsum([b - a for a, b in sl])]).astype(np.int64)
+            ys = [self.y_local[int(offs[i]):int(offs[i + 1])] for i in range(len(sl))]
+            self.step = rb.RansStep(self.mats, xs, ys, lib=lib)
+            # rank r's local buffer holds its rows of every projection in order
+            self._counts = [sum(self.layout.nrows[i][r] for i in range(len(sl))) for r in range(self.world)]
+            self.gathered = None
+            self.full = None
+
+    @property
+    def kernels(self) -> int:
+        return self.step.kernels
+
+    def __call__(self):
+        self.step()
+        if self.exchange == "fused":
+            # every rank's rows are in every rank's buffer once all ranks have
+            # passed this barrier (it raises after timeout_ms)
+            self.hdl.barrier(channel=0, timeout_ms=self.timeout_ms)
+        else:
+            self.gathered = gather_rows(self.y_local, self._counts)
+        return self.full
+
+    def full_outputs(self):
+        """Complete outputs of every projection (a copy for the nccl exchange)."""
+        if self.exchange == "fused":
+            return self.full
+        return regroup_rank_major(self.gathered, self.layout)
+
+    def close(self):
+        """Drop the plan and the symmetric-memory handle before the process
+        group is destroyed."""
+        self.step = None
+        self.hdl = None
