@@ -874,7 +874,7 @@ static int sm_count() {
     return n;
 }
 
-// Most symbols one staged pass should hold: 85% of the stage at the matrix's
+// Most symbols one staged pass should hold: 90% of the stage at the matrix's
 // mean size per symbol (state words included) when the buffer length is
 // known, else a bound for up to ~5.3 bits/symbol.  A pass whose span still
 // does not fit is decoded from global memory (same results, slower).
@@ -882,7 +882,7 @@ static int64_t pass_symbols(const MatDev& d) {
     if (kStageBytes <= 0) return 12288;
     if (d.nwords > 0 && d.rows > 0 && d.cols > 0) {
         const double bytes_per_symbol = 2.0 * (double)d.nwords / ((double)d.rows * (double)d.cols);
-        return std::max<int64_t>(1, (int64_t)(0.85 * kStageBytes / bytes_per_symbol));
+        return std::max<int64_t>(1, (int64_t)(0.9 * kStageBytes / bytes_per_symbol));
     }
     return (int64_t)kStageBytes * 3 / 2;
 }
@@ -1102,6 +1102,15 @@ static int launch_decode_t(const MatDev& d, void* out, cudaStream_t stream) {
     return (int)cudaGetLastError();
 }
 
+template <int R>
+static int launch_decode_k(const MatDev& d, void* out, int k, cudaStream_t stream) {
+    switch (k) {
+        case 4: return launch_decode_t<R, 4>(d, out, stream);
+        case 3: return launch_decode_t<R, 3>(d, out, stream);
+        default: return launch_decode_t<R, 2>(d, out, stream);
+    }
+}
+
 extern "C" int launch_rans_decode(int R, const void* words, const void* offs, const void* table,
                                   const void* step, void* out, int rows, int cols, int C,
                                   cudaStream_t stream) {
@@ -1112,12 +1121,17 @@ extern "C" int launch_rans_decode(int R, const void* words, const void* offs, co
     d.nrb = rows / R;
     d.nk = C / 32;
     d.tail_words = 2 + R * d.nk;
+    // tiles per warp pass: as many as the stage holds (2..4), while the
+    // matrix still gives two waves of warps; small matrices keep K = 2
+    const int64_t ntiles = (int64_t)d.nrb * d.ncb;
+    int64_t k = std::min<int64_t>(4, std::max<int64_t>(2, pass_symbols(d) / ((int64_t)R * C)));
+    while (k > 2 && ntiles / k < 2 * (int64_t)split_target()) --k;
     switch (R) {
-        case 1: return launch_decode_t<1, 2>(d, out, stream);
-        case 2: return launch_decode_t<2, 2>(d, out, stream);
-        case 4: return launch_decode_t<4, 2>(d, out, stream);
-        case 8: return launch_decode_t<8, 2>(d, out, stream);
-        case 16: return launch_decode_t<16, 2>(d, out, stream);
+        case 1: return launch_decode_k<1>(d, out, (int)k, stream);
+        case 2: return launch_decode_k<2>(d, out, (int)k, stream);
+        case 4: return launch_decode_k<4>(d, out, (int)k, stream);
+        case 8: return launch_decode_k<8>(d, out, (int)k, stream);
+        case 16: return launch_decode_k<16>(d, out, (int)k, stream);
         default: return -1;
     }
 }
