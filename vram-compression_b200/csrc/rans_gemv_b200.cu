@@ -61,10 +61,17 @@ constexpr int kPadWords = 8;
 #ifndef RB_LAYOUT
 #define RB_LAYOUT 1      // shared-memory table entry: 0 = sym|bias<<8|freq<<20, 1 = bias|sym<<12|freq<<20
 #endif
+#ifndef RB_I4_UNROLL
+#define RB_I4_UNROLL 2   // int4 baseline: column groups in flight per lane
+#endif
+#ifndef RB_I4_WAVES
+#define RB_I4_WAVES 2    // int4 baseline: rows per warp leave at least this many waves of warps
+#endif
 #ifndef RB_ALIGNTAB
 #define RB_ALIGNTAB 1    // place the table at a 16 KB-aligned shared address (address = one LOP3)
 #endif
 constexpr int kWarps = RB_WARPS;          // warps per CTA
+constexpr int kI4Unroll = RB_I4_UNROLL;
 constexpr int kThreads = kWarps * 32;
 constexpr int kStageBytes = RB_STAGE_BYTES;  // per-warp staging buffer (0: no staging)
 constexpr int kTableBytes = kProbM * 4;
@@ -821,11 +828,13 @@ __global__ void __launch_bounds__(kThreads, RB_MINB) decode_kernel(MatDev d, __n
 // Fixed-rate int4 baseline.  A warp owns kInt4Rows consecutive rows: lane l
 // reads the 8-code words g = l, l+32, ... of every row (32-bit loads, 128 B
 // per warp and row, coalesced) and the 8 activations of group g once for all
-// its rows, so x traffic is 1/kInt4Rows of the weight traffic.  A nibble q
-// becomes the float 2^23 + q by one logic op (0x4b000000 | q) and one FADD
-// removes 2^23 + 8.  The kInt4Rows partial sums are transpose-reduced.  The
-// launcher picks kInt4Rows in {8,4,2,1} so that small matrices still get
-// enough warps.
+// its rows.  Nibble b of a word becomes an exact float with one LOP3 and one
+// FADD, without a shift: (q & 0xF << 4b) | 0x4B000000 is the float
+// 2^23 + n * 16^b (exact while the nibble stays below bit 23, b <= 4), and
+// subtracting 2^23 + 8 * 16^b leaves (n - 8) * 16^b; the activation of that
+// column is pre-multiplied by 16^-b (a power of two: exact), once per group
+// for all rows.  Nibbles 5..7 use q >> 20 the same way (b = 0..2).  The
+// kInt4Rows partial sums are transpose-reduced.
 template <int kInt4Rows>
 __global__ void __launch_bounds__(256) int4_gemv_kernel(const uint32_t* __restrict__ w,
                                                         const float4* __restrict__ x,
@@ -841,21 +850,31 @@ __global__ void __launch_bounds__(256) int4_gemv_kernel(const uint32_t* __restri
     float acc[kInt4Rows];
 #pragma unroll
     for (int r = 0; r < kInt4Rows; ++r) acc[r] = 0.f;
-#pragma unroll 2
+    // per nibble position: scale of the activation, float offset, mask
+    constexpr float kScale[8] = {1.f, 0.0625f, 0.00390625f, 0.000244140625f, 1.52587890625e-05f,
+                                 1.f, 0.0625f, 0.00390625f};
+#pragma unroll kI4Unroll
     for (int g = lane; g < ngroup; g += 32) {
         const float4 x0 = __ldg(x + 2 * g);
         const float4 x1 = __ldg(x + 2 * g + 1);
-        const float xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+        const float xv[8] = {x0.x * kScale[0], x0.y * kScale[1], x0.z * kScale[2], x0.w * kScale[3],
+                             x1.x * kScale[4], x1.y * kScale[5], x1.z * kScale[6], x1.w * kScale[7]};
         uint32_t q[kInt4Rows];
 #pragma unroll
         for (int r = 0; r < kInt4Rows; ++r) q[r] = __ldg(wr[r] + g);
 #pragma unroll
-        for (int r = 0; r < kInt4Rows; ++r)
+        for (int r = 0; r < kInt4Rows; ++r) {
+            const uint32_t qh = q[r] >> 20;
 #pragma unroll
             for (int b = 0; b < 8; ++b) {
-                const float c = __int_as_float(((q[r] >> (4 * b)) & 15u) | 0x4B000000u) - 8388616.0f;
+                const int s = b < 5 ? b : b - 5;
+                const uint32_t src = b < 5 ? q[r] : qh;
+                const uint32_t bits = (src & (0xFu << (4 * s))) | 0x4B000000u;
+                const float off = 8388608.0f + 8.0f * static_cast<float>(1u << (4 * s));
+                const float c = __int_as_float(bits) - off;
                 acc[r] = fmaf(c, xv[b], acc[r]);
             }
+        }
     }
     const float s = reduce_scatter<kInt4Rows>(acc, lane);
     constexpr int kShift = 5 - Log2<kInt4Rows>::value;
@@ -1140,7 +1159,9 @@ extern "C" int launch_int4_gemv(const void* w, const void* x, void* y, int rows,
                                 cudaStream_t stream) {
     if (rows <= 0 || cols <= 0 || cols % 32) return -2;
     const int threads = 256;
-    const int64_t want = split_target();
+    // rows per warp: the most that still leaves RB_I4_WAVES waves of warps
+    // (memory latency needs them), else one
+    const int64_t want = RB_I4_WAVES * split_target();
     const int rw = rows / 8 >= want ? 8 : rows / 4 >= want ? 4 : rows / 2 >= want ? 2 : 1;
     const int64_t warps = (rows + rw - 1) / rw;
     const int grid = (int)((warps * 32 + threads - 1) / threads);
