@@ -690,7 +690,7 @@ __global__ void __launch_bounds__(kThreads, RB_MINB) gemv_step_kernel(const Step
 // One symbol of a staged stream returning kCodeScale*code (no FMA): the
 // decode-to-dense path.  Same sequence as sym_step_ptx.
 __device__ __forceinline__ float sym_code(uint32_t& st, uint32_t& w, uint32_t& pw, uint32_t tb, const uint32_t* tab,
-                                          bool staged, const MatDev& d) {
+                                          bool staged, const MatDev& d, uint32_t magic) {
 #if RB_LAYOUT == 1 && RB_ALIGNTAB
     if (staged) {
         float c;
@@ -707,11 +707,10 @@ __device__ __forceinline__ float sym_code(uint32_t& st, uint32_t& w, uint32_t& p
             "@p prmt.b32 %0, %1, %0, 0x5410;\n\t"
             "@p add.u32 %2, %2, 2;\n\t"
             "@p ld.shared.u16 %1, [%2];\n\t"
-            "and.b32 t, e, 0x000FF000;\n\t"
-            "or.b32 t, t, 0x4B000000;\n\t"
+            "lop3.b32 t, e, 0x000FF000, %5, 0xEA;\n\t"
             "sub.f32 %3, t, 0f4B080000;\n\t}"
             : "+r"(st), "+r"(w), "+r"(pw), "=f"(c)
-            : "r"(tb));
+            : "r"(tb), "r"(magic));
         return c;
     }
 #endif
@@ -752,23 +751,33 @@ __device__ __forceinline__ void decode_store(const MatDev& d, const uint32_t (&p
             w[j] = __ldg(d.words + p[j]);
         }
     }
-    const int cols = d.cols;
+    const uint32_t magic = __shfl_sync(0xffffffffu, 0x4B000000u, 0);   // kept in a register
+    // element offsets of the tile's rows (R x cols < 2^32 elements: checked by the launcher)
+    uint32_t roff[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) roff[r] = (uint32_t)r * (uint32_t)d.cols;
     for (int k = 0; k < d.nk; ++k) {
         float sv[K];
+        __nv_bfloat16* o[K];
 #pragma unroll
-        for (int j = 0; j < K; ++j) sv[j] = __ldg(d.step + col0[j] + 32 * k) * kInvCodeScale;
+        for (int j = 0; j < K; ++j) {
+            sv[j] = __ldg(d.step + col0[j] + 32 * k) * kInvCodeScale;
+            o[j] = orow[j] + 32 * k;
+        }
 #pragma unroll
         for (int r = 0; r < R; ++r) {
 #pragma unroll
             for (int j = 0; j < K; ++j) {
                 float c;
                 if (ptx) {
-                    c = sym_code(st[j], w[j], p[j], sm.tab_s, sm.tab, true, d);
+                    c = sym_code(st[j], w[j], p[j], sm.tab_s, sm.tab, true, d, magic);
                 } else {
                     // generic pointer bookkeeping of the C++ step uses offsets from g_smem
-                    c = sym_code(st[j], w[j], p[j], sm.tab_s, sm.tab, STAGED, d);
+                    c = sym_code(st[j], w[j], p[j], sm.tab_s, sm.tab, STAGED, d, magic);
                 }
-                if (j < kk) orow[j][(int64_t)r * cols + 32 * k] = __float2bfloat16(c * sv[j]);
+                // no branch on j < kk: a slot past kk replays tile kk-1 and
+                // stores the same values to the same place
+                o[j][roff[r]] = __float2bfloat16(c * sv[j]);
             }
         }
     }
@@ -1135,6 +1144,7 @@ extern "C" int launch_rans_decode(int R, const void* words, const void* offs, co
                                   cudaStream_t stream) {
     if (!valid_R(R)) return -1;
     if (!shape_ok(R, rows, cols, C)) return -2;
+    if ((int64_t)R * cols >= (int64_t(1) << 32)) return -2;   // row offsets of a tile are 32-bit
     MatDev d = make_desc(words, offs, table, nullptr, step, nullptr, rows, cols, C, -1);
     d.ncb = cols / C;
     d.nrb = rows / R;
