@@ -240,3 +240,28 @@ def test_throughput_step_prescale_reads_fresh_activations(torch, rb):
     torch.cuda.synchronize()
     for x, y, codes, step in zip(xs, ys, codes_l, steps):
         _check_y(y.cpu().numpy(), _y64(codes, step, x.float().cpu().numpy()))
+
+
+def test_medium_launch_segments_rows(torch, rb):
+    """A launch of a few waves of whole-row items (8 down projections,
+    1536 x 8960: 1536 row blocks of 7 two-tile passes) is cut into row
+    segments that meet in the workspace; results must not change, including
+    when the step is launched repeatedly (counters reset themselves)."""
+    codes = orc.synth_codes(1536, 8960, 4.25, "gauss", seed=41)
+    enc = rb.encode(codes, 8, 640)
+    mats, xs, ys, steps = [], [], [], []
+    for i in range(8):
+        step = (0.01 * np.random.default_rng(200 + i).uniform(0.5, 1.5, 8960)).astype(np.float32)
+        mats.append(rb.RansMatrix(enc, torch.from_numpy(step)))
+        xs.append(torch.from_numpy(np.random.default_rng(300 + i).standard_normal(8960).astype(np.float32))
+                  .bfloat16().cuda())
+        ys.append(torch.full((1536,), float("nan"), device="cuda"))
+        steps.append(step)
+    st = rb.RansStep(mats, xs, ys)
+    for _ in range(3):
+        for y in ys:
+            y.fill_(float("nan"))
+        st()
+    torch.cuda.synchronize()
+    for x, y, step in zip(xs, ys, steps):
+        _check_y(y.cpu().numpy(), _y64(codes, step, x.float().cpu().numpy()))

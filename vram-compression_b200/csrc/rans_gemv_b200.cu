@@ -1276,6 +1276,24 @@ static int layout_step(const RansGemvDesc* descs, int n, int R, StepLayout& L) {
                 npartials += (int64_t)d.nrb * d.nseg * R;
             }
         }
+    } else if (items < 16 * (int64_t)split_target()) {
+        // A launch of a few waves of whole-row items loses up to one wave to
+        // quantisation (e.g. 3.03 waves run as 4).  Give each column-mode
+        // matrix a share of the resident warps in proportion to its items and
+        // let the makespan model of plan_matrix cut its rows into equal
+        // segments of passes (same K); segments meet in `partials`, as above.
+        const int64_t W = split_target();
+        for (MatDev& d : L.mats) {
+            if (d.rowmode || d.ncb <= d.kcol) continue;
+            const int share = (int)std::max<int64_t>(1, W * d.nitems / items);
+            MatDev sp = d;
+            plan_matrix(sp, R, share);
+            if (sp.nseg <= 1 || sp.kcol != d.kcol) continue;
+            d = sp;
+            d.accumulate = 0;
+            ncounters += d.nrb;
+            npartials += (int64_t)d.nrb * d.nseg * R;
+        }
     }
     for (MatDev& d : L.mats) L.nchunks += (d.nitems + kWarps - 1) / kWarps;
     // Launches of two or more waves of items read activations through a
