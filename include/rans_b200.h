@@ -36,7 +36,7 @@ extern "C" {
 typedef struct CUstream_st* cudaStream_t;
 #endif
 
-#define RANS_B200_ABI_VERSION 1
+#define RANS_B200_ABI_VERSION 2   /* 2: escape-code entry points, rans_gemv_step_kernels */
 
 /* ---------------------------------------------------------------- drop-in
  * The three entry points of the reference library, same names, argument

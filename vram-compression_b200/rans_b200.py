@@ -30,7 +30,7 @@ M = 1 << SCALE_BITS
 RANS_L = 1 << 16
 OFFSET = 128
 PAD_WORDS = 8
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 _vp, _i32, _i64, _sz = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_size_t
 
