@@ -940,7 +940,14 @@ static void plan_matrix(MatDev& d, int R, int split_for) {
     int k = 1;
     for (int c = kmax; c >= 2; --c)
         if (d.ncb % c == 0) { k = c; break; }
-    if (k == 1 && kmax >= 2 && d.ncb > 1) k = std::min(kmax, std::min(d.ncb, 3));   // no divisor: accept idle slots
+    if (k == 1 && kmax >= 2 && d.ncb > 1) {
+        // no divisor: accept idle stream slots in the last pass only when they
+        // are at most 1/8 of all slots (K = 2 over 3 tiles wastes 1/4: slower)
+        for (int c = std::min(kmax, d.ncb); c >= 2; --c) {
+            const int passes = (d.ncb + c - 1) / c;
+            if ((passes * c - d.ncb) * 8 <= passes * c) { k = c; break; }
+        }
+    }
     // A small matrix that may be split is latency-bound: one tile per warp
     // gives the most independent warps (the serial chain of one stream is the
     // floor either way).
