@@ -95,7 +95,6 @@ struct MatDev {
     int64_t wlimit;        // nwords < 0: words readable from `words` on (to the end of its
                            // device allocation), 0 = unknown
     int rows, cols, C, ncb, nrb, nk;
-    int rowmode;           // 1: ncb == 1, item = KROW row blocks
     int kcol;              // column-mode streams per lane (2..4)
     int nseg, cbs;         // column-mode segments per row block, cbs per segment
     int nitems;
@@ -522,50 +521,14 @@ __device__ __forceinline__ void colmode_epilogue(const MatDev& d, int rb, int se
     }
 }
 
-// Row mode (ncb == 1): KR consecutive row blocks, one stream each per lane.
-template <int R, int KR, bool BF16X>
-__device__ void rowmode_item(const MatDev& d, int item, const uint32_t* tab, uint16_t* stage,
-                             int lane, int& bad) {
-    const int rb0 = item * KR;
-    const int kk = min(KR, d.nrb - rb0);
-    float acc[KR][R];
-#pragma unroll
-    for (int j = 0; j < KR; ++j)
-#pragma unroll
-        for (int r = 0; r < R; ++r) acc[j][r] = 0.f;
-    int xcol[KR];
-#pragma unroll
-    for (int j = 0; j < KR; ++j) xcol[j] = lane;
-    run_pass<R, KR, KR, BF16X>(d, tab, stage, rb0, kk, xcol, acc, bad, lane);
-    float* flat = &acc[0][0];
-    float v[KR * R];
-#pragma unroll
-    for (int i = 0; i < KR * R; ++i) v[i] = flat[i];
-    const float s = reduce_scatter<KR * R>(v, lane) * kInvCodeScale;
-    constexpr int kShift = 5 - Log2<KR * R>::value;
-    const int idx = lane >> kShift;          // = j*R + r
-    if ((lane & ((1 << kShift) - 1)) == 0 && idx / R < kk) {
-        const int row = (rb0 + idx / R) * R + idx % R;
-        if (d.npeer > 0) store_peers(d, row, s);
-        else d.y[row] = s;
-    }
-}
-
-template <int R>
-struct RowK { static constexpr int value = (R >= 8) ? 32 / R : 4; };
-
 template <int R, bool BF16X>
 __device__ __forceinline__ void process_item(const MatDev& d, int item, const uint32_t* tab,
                                              uint16_t* stage, int lane, int& bad) {
-    if (d.rowmode) {
-        rowmode_item<R, RowK<R>::value, BF16X>(d, item, tab, stage, lane, bad);
-    } else {
-        switch (d.kcol) {
-            case 1: colmode_item<R, 1, BF16X>(d, item, tab, stage, lane, bad); break;
-            case 2: colmode_item<R, 2, BF16X>(d, item, tab, stage, lane, bad); break;
-            case 3: colmode_item<R, 3, BF16X>(d, item, tab, stage, lane, bad); break;
-            default: colmode_item<R, 4, BF16X>(d, item, tab, stage, lane, bad); break;
-        }
+    switch (d.kcol) {
+        case 1: colmode_item<R, 1, BF16X>(d, item, tab, stage, lane, bad); break;
+        case 2: colmode_item<R, 2, BF16X>(d, item, tab, stage, lane, bad); break;
+        case 3: colmode_item<R, 3, BF16X>(d, item, tab, stage, lane, bad); break;
+        default: colmode_item<R, 4, BF16X>(d, item, tab, stage, lane, bad); break;
     }
 }
 
@@ -590,16 +553,10 @@ __global__ void __launch_bounds__(kThreads, RB_MINB) gemv_matrix_kernel(MatDev d
 }
 
 // Tiles [t_begin, t_end) of a work item (consecutive in stream order).
-__device__ __forceinline__ void item_tiles(const MatDev& d, int R, int item, int64_t& t_begin, int64_t& t_end) {
-    if (d.rowmode) {
-        const int kr = R >= 8 ? 32 / R : 4;
-        t_begin = (int64_t)item * kr;
-        t_end = min((int64_t)d.nrb, t_begin + kr);
-    } else {
-        const int rb = item / d.nseg, seg = item - rb * d.nseg;
-        t_begin = (int64_t)rb * d.ncb + seg * d.cbs;
-        t_end = (int64_t)rb * d.ncb + min(d.ncb, seg * d.cbs + d.cbs);
-    }
+__device__ __forceinline__ void item_tiles(const MatDev& d, int item, int64_t& t_begin, int64_t& t_end) {
+    const int rb = item / d.nseg, seg = item - rb * d.nseg;
+    t_begin = (int64_t)rb * d.ncb + seg * d.cbs;
+    t_end = (int64_t)rb * d.ncb + min(d.ncb, seg * d.cbs + d.cbs);
 }
 
 // Activation prescale of a throughput step: out[c] = float(x_bf16[c]) * step[c]
@@ -636,8 +593,8 @@ __global__ void fill_spans_kernel(const StepHeader* __restrict__ hdr, int R) {
     const Chunk ch = chunks[c];
     const MatDev& d = descs[ch.desc];
     int64_t t0, t1, u0, u1;
-    item_tiles(d, R, ch.item0, t0, t1);
-    item_tiles(d, R, ch.item0 + ch.nitems - 1, u0, u1);
+    item_tiles(d, ch.item0, t0, t1);
+    item_tiles(d, ch.item0 + ch.nitems - 1, u0, u1);
     const uint32_t w0 = d.offs[t0 * 32];
     const uint64_t w1 = span_end(d, u1 * 32);
     spans[c] = make_uint2(w0, w1 == UINT64_MAX ? w0 : static_cast<uint32_t>(w1));
@@ -894,7 +851,6 @@ __global__ void __launch_bounds__(256) int4_gemv_kernel(const uint32_t* __restri
 // ------------------------------------------------------------ host side
 static bool valid_R(int R) { return R == 1 || R == 2 || R == 4 || R == 8 || R == 16; }
 
-static int row_k(int R) { return R >= 8 ? 32 / R : 4; }
 
 static int sm_count() {
     int dev = 0, n = 148;
@@ -923,16 +879,12 @@ static void plan_matrix(MatDev& d, int R, int split_for) {
     d.nrb = d.rows / R;
     d.nk = d.C / 32;
     d.tail_words = 2 + R * d.nk;
-    d.rowmode = d.ncb == 1 ? 1 : 0;
     d.accumulate = 0;
-    if (d.rowmode) {
-        const int kr = row_k(R);
-        d.kcol = 0;
-        d.nseg = 1;
-        d.cbs = 1;
-        d.nitems = (d.nrb + kr - 1) / kr;
-        return;
-    }
+    // Every matrix is decoded in column mode, a matrix of one column block
+    // (cols == C) included: K = 1, one tile per pass.  (Decoding several row
+    // blocks of such a matrix as interleaved streams of one pass measured 1.5
+    // to 3.5 times slower on B200: larger spans that fall out of the stage,
+    // a 32-value reduction and activations reloaded per stream.)
     // K that divides ncb (no idle stream slots), preferring more streams per
     // lane, with at most pass_symbols(d) symbols per pass so that the pass's
     // words fit the stage.
@@ -1100,7 +1052,7 @@ extern "C" int rans_gemv_bf16(int R, const void* words, const void* offs, const 
     if (!shape_ok(R, rows, cols, C) || step == nullptr) return -2;
     MatDev d = make_desc(words, offs, table, x_bf16, step, y, rows, cols, C, nwords);
     plan_matrix(d, R, 0);   // whole row blocks per warp: y is stored, no atomics
-    if (!d.rowmode) {   // (row mode has kcol = 0 and is never split)
+    {
         // Splitting the column blocks of a row block across warps (and
         // accumulating into a zeroed y) pays when whole rows give too few
         // warps (e.g. a 1536 x 8960 down projection), or when it shortens the
@@ -1248,7 +1200,7 @@ static int layout_step(const RansGemvDesc* descs, int n, int R, StepLayout& L) {
         int64_t total = 0;
         for (size_t i = 0; i < L.mats.size(); ++i) {
             const MatDev& d = L.mats[i];
-            if (!d.rowmode && d.ncb > 1) T[i] = 1;
+            if (d.ncb > 1) T[i] = 1;
             total += T[i] ? (int64_t)d.nrb * d.ncb : d.nitems;
         }
         auto next_t = [&](size_t i) {
@@ -1291,7 +1243,7 @@ static int layout_step(const RansGemvDesc* descs, int n, int R, StepLayout& L) {
         // segments of passes (same K); segments meet in `partials`, as above.
         const int64_t W = split_target();
         for (MatDev& d : L.mats) {
-            if (d.rowmode || d.ncb <= d.kcol) continue;
+            if (d.ncb <= d.kcol) continue;
             const int share = (int)std::max<int64_t>(1, W * d.nitems / items);
             MatDev sp = d;
             plan_matrix(sp, R, share);
@@ -1440,7 +1392,7 @@ static int plan_step(const RansGemvDesc* descs, const void* const* peer_y, int n
     // Longest chunks first: CTAs start in blockIdx order, so the grid's last
     // wave holds the shortest chunks and the tail stays short.
     auto item_cost = [&](const MatDev& d) -> int64_t {
-        return d.rowmode ? (int64_t)row_k(R) * R * d.cols : (int64_t)R * d.cbs * d.C;
+        return (int64_t)R * d.cbs * d.C;
     };
     std::stable_sort(ch, ch + nchunks, [&](const Chunk& a, const Chunk& b) {
         return item_cost(md[a.desc]) > item_cost(md[b.desc]);
@@ -1616,7 +1568,7 @@ extern "C" int rans_gemv_step_noalloc(const RansGemvDesc* descs, int n, int R, c
     // same order as rans_gemv_step_plan (longest chunks first, ties in input
     // order), with an in-place sort
     auto item_cost = [&](const MatDev& d) -> int64_t {
-        return d.rowmode ? (int64_t)row_k(R) * R * d.cols : (int64_t)R * d.cbs * d.C;
+        return (int64_t)R * d.cbs * d.C;
     };
     std::sort(ch, ch + nchunks, [&](const Chunk& a, const Chunk& b) {
         const int64_t ca = item_cost(md[a.desc]), cb = item_cost(md[b.desc]);
