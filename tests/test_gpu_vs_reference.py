@@ -25,6 +25,7 @@ SHAPES = [  # rows, cols, R, C, dist, bits
     (1536, 8960, 8, 640, "gauss", 4.25),      # config 2 down
     (28672, 8192, 8, 512, "laplace", 2.25),   # config 5 gate/up
     (8192, 28672, 8, 512, "laplace", 2.25),   # config 5 down
+    (1536, 1536, 8, 1536, "laplace", 3.25),   # one column block (C = cols), as the reference's sweep picks
 ]
 
 
