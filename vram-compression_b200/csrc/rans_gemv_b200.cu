@@ -18,7 +18,7 @@
 //       bias | sym << 12 | freq << 20
 //     so the entry address is one shift + one LOP3, freq one shift, bias one
 //     mask, and 4096*code one LOP3 + FADD (the float 2^23 + 4096*sym);
-//   * fp32 accumulation; the R (or K*R) partial sums per lane are combined with
+//   * fp32 accumulation; the R partial sums per lane are combined with
 //     a transpose-reduce (reduce-scatter) butterfly, R-1 + log2(32/R) shuffles
 //     instead of 5*R, and stored without atomics whenever a warp covers every
 //     column block of its rows.
@@ -101,7 +101,8 @@ struct MatDev {
     int accumulate;        // 1: atomicAdd into y (split rows), 0: store
     int npeer;             // > 0: store every output row to all of ypeer[] instead of y
     int tail_words;        // most words one stream can hold: 2 state words + one per symbol
-    int pad_;
+    int combine;           // 1: the nseg segments of a row block are consecutive warps of one
+                           // CTA and add up in shared memory (step kernel, one item per warp)
     float* ypeer[kMaxPeers];   // the same rows of every rank's output buffer (peer addresses)
     float* partials;       // nseg > 1 without accumulate: [nrb][nseg][R] segment sums (workspace)
     uint32_t* counters;    // [nrb] arrivals per row block, zero between launches (workspace)
@@ -464,11 +465,12 @@ __device__ __forceinline__ void store_peers(const MatDev& d, int row, float s) {
 
 // Column mode: rows rb*R..rb*R+R-1, column blocks of segment `seg`.
 template <int R>
-__device__ __forceinline__ void colmode_epilogue(const MatDev& d, int rb, int seg, float s, int lane);
+__device__ __forceinline__ void colmode_epilogue(const MatDev& d, int rb, int seg, float s, int lane,
+                                                 uint16_t* stage, int warp, int nactive);
 
 template <int R, int K, bool BF16X>
 __device__ void colmode_item(const MatDev& d, int item, const uint32_t* tab, uint16_t* stage,
-                             int lane, int& bad) {
+                             int lane, int& bad, int warp, int nactive) {
     const int rb = item / d.nseg;
     const int seg = item - rb * d.nseg;
     const int cb_begin = seg * d.cbs;
@@ -483,17 +485,32 @@ __device__ void colmode_item(const MatDev& d, int item, const uint32_t* tab, uin
         for (int j = 0; j < K; ++j) xcol[j] = (cb0 + (j < kk ? j : 0)) * d.C + lane;
         run_pass<R, K, 1, BF16X>(d, tab, stage, (int64_t)rb * d.ncb + cb0, kk, xcol, acc, bad, lane);
     }
-    colmode_epilogue<R>(d, rb, seg, reduce_scatter<R>(acc[0], lane) * kInvCodeScale, lane);
+    colmode_epilogue<R>(d, rb, seg, reduce_scatter<R>(acc[0], lane) * kInvCodeScale, lane, stage, warp, nactive);
 }
 
 // Output of one column-mode item: lane l holds the full 32-lane sum s of row
 // rb*R + (l >> (5 - log2 R)).
 template <int R>
-__device__ __forceinline__ void colmode_epilogue(const MatDev& d, int rb, int seg, float s, int lane) {
+__device__ __forceinline__ void colmode_epilogue(const MatDev& d, int rb, int seg, float s, int lane,
+                                                 uint16_t* stage, int warp, int nactive) {
     constexpr int kShift = 5 - Log2<R>::value;
     const bool owner = (lane & ((1 << kShift) - 1)) == 0;
     const int r = lane >> kShift;
-    if (d.nseg > 1 && d.partials != nullptr) {
+    if (d.combine) {
+        // The row block's segments are warps warp-seg .. warp-seg+nseg-1 of
+        // this CTA: each leaves its R sums in its own stage (free after its
+        // passes), one named barrier over the CTA's nactive working warps
+        // (each reaches it once), and the segment-0 warp adds them in
+        // segment order (deterministic).  No global fence or atomic.
+        if (owner) reinterpret_cast<float*>(stage)[r] = s;
+        asm volatile("bar.sync 1, %0;\n" ::"r"(nactive * 32) : "memory");
+        if (seg != 0) return;
+        if (owner) {
+            float t = 0.f;
+            for (int g = 0; g < d.nseg; ++g) t += reinterpret_cast<const float*>(smem_map(warp + g).stage)[r];
+            s = t;
+        }
+    } else if (d.nseg > 1 && d.partials != nullptr) {
         // Row block split over nseg warps: publish this segment's R sums, and
         // let the last warp to finish add all segments in segment order
         // (deterministic) and store y.  The counter is reset for the next launch.
@@ -521,14 +538,16 @@ __device__ __forceinline__ void colmode_epilogue(const MatDev& d, int rb, int se
     }
 }
 
+// warp / nactive: this warp's index and the CTA's number of working warps
+// (used only when d.combine is set: the step kernel, one item per warp).
 template <int R, bool BF16X>
 __device__ __forceinline__ void process_item(const MatDev& d, int item, const uint32_t* tab,
-                                             uint16_t* stage, int lane, int& bad) {
+                                             uint16_t* stage, int lane, int& bad, int warp, int nactive) {
     switch (d.kcol) {
-        case 1: colmode_item<R, 1, BF16X>(d, item, tab, stage, lane, bad); break;
-        case 2: colmode_item<R, 2, BF16X>(d, item, tab, stage, lane, bad); break;
-        case 3: colmode_item<R, 3, BF16X>(d, item, tab, stage, lane, bad); break;
-        default: colmode_item<R, 4, BF16X>(d, item, tab, stage, lane, bad); break;
+        case 1: colmode_item<R, 1, BF16X>(d, item, tab, stage, lane, bad, warp, nactive); break;
+        case 2: colmode_item<R, 2, BF16X>(d, item, tab, stage, lane, bad, warp, nactive); break;
+        case 3: colmode_item<R, 3, BF16X>(d, item, tab, stage, lane, bad, warp, nactive); break;
+        default: colmode_item<R, 4, BF16X>(d, item, tab, stage, lane, bad, warp, nactive); break;
     }
 }
 
@@ -549,7 +568,7 @@ __global__ void __launch_bounds__(kThreads, RB_MINB) gemv_matrix_kernel(MatDev d
     // and is the slowest, so it starts in the first wave.
     int bad = 0;
     for (int i = blockIdx.x * kWarps + warp; i < d.nitems; i += gridDim.x * kWarps)
-        process_item<R, BF16X>(d, d.nitems - 1 - i, tab, stage, lane, bad);
+        process_item<R, BF16X>(d, d.nitems - 1 - i, tab, stage, lane, bad, warp, 0);
 }
 
 // Tiles [t_begin, t_end) of a work item (consecutive in stream order).
@@ -640,8 +659,8 @@ __global__ void __launch_bounds__(kThreads, RB_MINB) gemv_step_kernel(const Step
     if (warp >= ch.nitems) return;
     int bad = 0;
     const MatDev dl = d;
-    if (dl.step != nullptr) process_item<R, true>(dl, ch.item0 + warp, tab, stage, lane, bad);
-    else process_item<R, false>(dl, ch.item0 + warp, tab, stage, lane, bad);
+    if (dl.step != nullptr) process_item<R, true>(dl, ch.item0 + warp, tab, stage, lane, bad, warp, ch.nitems);
+    else process_item<R, false>(dl, ch.item0 + warp, tab, stage, lane, bad, warp, ch.nitems);
 }
 
 // One symbol of a staged stream returning kCodeScale*code (no FMA): the
@@ -1180,6 +1199,10 @@ struct StepLayout {
 
 static size_t align16(size_t v) { return (v + 15) & ~size_t(15); }
 
+// Items per CTA of the step kernel: 8, or whole row blocks when the segments
+// of a row block add up in shared memory.
+static int chunk_items(const MatDev& d) { return d.combine ? (kWarps / d.nseg) * d.nseg : kWarps; }
+
 static int layout_step(const RansGemvDesc* descs, int n, int R, StepLayout& L) {
     L.mats.clear();
     if (count_chunks(descs, n, R, &L.mats) < 0) return -2;
@@ -1230,7 +1253,11 @@ static int layout_step(const RansGemvDesc* descs, int n, int R, StepLayout& L) {
             d.cbs = T[i];
             d.nitems = d.nrb * d.nseg;
             d.accumulate = 0;
-            if (d.nseg > 1) {
+            // a launch this short is latency-bound: segments of a row block
+            // meet in shared memory when they fit one CTA (idle warps cost
+            // nothing here), else in global partials
+            d.combine = d.nseg > 1 && d.nseg <= kWarps ? 1 : 0;
+            if (d.nseg > 1 && !d.combine) {
                 ncounters += d.nrb;
                 npartials += (int64_t)d.nrb * d.nseg * R;
             }
@@ -1250,11 +1277,16 @@ static int layout_step(const RansGemvDesc* descs, int n, int R, StepLayout& L) {
             if (sp.nseg <= 1 || sp.kcol != d.kcol) continue;
             d = sp;
             d.accumulate = 0;
-            ncounters += d.nrb;
-            npartials += (int64_t)d.nrb * d.nseg * R;
+            // segments meet in shared memory when whole row blocks fill a CTA
+            // exactly (no idle warps), else in global partials
+            d.combine = kWarps % d.nseg == 0 ? 1 : 0;
+            if (!d.combine) {
+                ncounters += d.nrb;
+                npartials += (int64_t)d.nrb * d.nseg * R;
+            }
         }
     }
-    for (MatDev& d : L.mats) L.nchunks += (d.nitems + kWarps - 1) / kWarps;
+    for (MatDev& d : L.mats) L.nchunks += (d.nitems + chunk_items(d) - 1) / chunk_items(d);
     // Launches of two or more waves of items read activations through a
     // prescaled fp32 copy (5% faster on a whole decoder step); shorter ones
     // skip the extra kernel, which would cost more than it saves.
@@ -1347,7 +1379,7 @@ static int plan_step(const RansGemvDesc* descs, const void* const* peer_y, int n
     uint8_t* ws = static_cast<uint8_t*>(workspace);
     int64_t coff = 0, poff = 0;
     for (MatDev& d : mats) {
-        if (d.nseg > 1 && !d.accumulate) {
+        if (d.nseg > 1 && !d.accumulate && !d.combine) {
             d.counters = reinterpret_cast<uint32_t*>(ws + L.counters_off) + coff;
             d.partials = reinterpret_cast<float*>(ws + L.partials_off) + poff;
             coff += d.nrb;
@@ -1381,10 +1413,11 @@ static int plan_step(const RansGemvDesc* descs, const void* const* peer_y, int n
     int64_t c = 0;
     for (int i = 0; i < n; ++i) {
         md[i] = mats[i];
-        for (int it = 0; it < mats[i].nitems; it += kWarps) {
+        const int cs = chunk_items(mats[i]);
+        for (int it = 0; it < mats[i].nitems; it += cs) {
             ch[c].desc = i;
             ch[c].item0 = it;
-            ch[c].nitems = mats[i].nitems - it < kWarps ? mats[i].nitems - it : kWarps;
+            ch[c].nitems = mats[i].nitems - it < cs ? mats[i].nitems - it : cs;
             ch[c].pad_ = 0;
             ++c;
         }
