@@ -265,3 +265,29 @@ def test_medium_launch_segments_rows(torch, rb):
     torch.cuda.synchronize()
     for x, y, step in zip(xs, ys, steps):
         _check_y(y.cpu().numpy(), _y64(codes, step, x.float().cpu().numpy()))
+
+
+@pytest.mark.parametrize("rows,cols,R,C,bits", [
+    (256, 8960, 8, 8960, 4.25),    # one tile of 71680 symbols per row block (C = cols)
+    (64, 4096, 16, 4096, 2.25),    # R = 16, C = cols
+    (512, 2048, 4, 2048, 5.0),     # R = 4, C = 2048
+])
+def test_tiles_larger_than_the_stage(torch, rb, rows, cols, R, C, bits):
+    """Tiles whose words exceed the 8 KB per-warp stage decode through windows
+    of each lane's stream: results match the oracle for the drop-in entry
+    (buffer length unknown), the bf16 entry (length known) and the step
+    launcher."""
+    codes = orc.synth_codes(rows, cols, bits, "gauss", seed=rows + C)
+    rng = np.random.default_rng(cols)
+    step = (0.01 * rng.uniform(0.5, 1.5, cols)).astype(np.float32)
+    x = rng.standard_normal(cols).astype(np.float32)
+    enc = rb.encode(codes, R, C)
+    m = rb.RansMatrix(enc, torch.from_numpy(step))
+    _check_y(m.gemv(torch.from_numpy(x).cuda()).cpu().numpy(), _y64(codes, step, x))
+    xb = torch.from_numpy(x).bfloat16()
+    yref = _y64(codes, step, xb.float().numpy())
+    _check_y(m.gemv_bf16(xb.cuda()).cpu().numpy(), yref)
+    y = torch.full((rows,), float("nan"), device="cuda")
+    rb.RansStep([m], [xb.cuda()], [y])()
+    torch.cuda.synchronize()
+    _check_y(y.cpu().numpy(), yref)

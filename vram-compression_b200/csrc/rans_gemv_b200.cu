@@ -427,6 +427,63 @@ __device__ __forceinline__ void decode_pass(const uint32_t (&pos)[K], const int 
         if (j < kk && st[j] != kRansL) ++bad;
 }
 
+// One-tile pass whose words do not fit the stage (large tiles: C of a few
+// thousand columns): windowed staging.  Each lane copies the next window of
+// its own stream -- kWinBytes from the 16-byte boundary at or below its read
+// position -- into its 1/32 of the stage, decodes up to 120 symbols with the
+// staged symbol step (at most one word per symbol, so the reads stay inside
+// the window), and refills.  Copies stop at `limit` (words readable from
+// d.words); words beyond the stream's end are never consumed.
+template <int R, bool BF16X>
+__device__ __forceinline__ void decode_pass_windowed(uint32_t pos, const int (&xcol)[1], const MatDev& d,
+                                                  float (&acc)[1][R], int& bad, uint16_t* stage, int lane,
+                                                  uint64_t limit) {
+    constexpr int kWinBytes = kStageBytes / 32;
+    constexpr int kWinWords = kWinBytes / 2;
+    constexpr int kChunkK = (kWinWords - 8) / R;   // head <= 7 words, then <= 1 word per symbol
+    static_assert(kChunkK >= 1, "stage too small for windowed staging");
+    const SmemMap sm = smem_map(0);
+    const uint32_t magic = __shfl_sync(0xffffffffu, 0x4B000000u, 0);
+    const uint32_t tb = sm.tab_s;
+    uint8_t* const wgen = reinterpret_cast<uint8_t*>(stage) + lane * kWinBytes;   // this lane's window
+    const uint32_t win = static_cast<uint32_t>(__cvta_generic_to_shared(wgen));
+    const uintptr_t wbase = reinterpret_cast<uintptr_t>(d.words);
+    const uintptr_t wend = wbase + 2ull * limit;
+    uint32_t st = (static_cast<uint32_t>(__ldg(d.words + pos)) << 16) | __ldg(d.words + pos + 1);
+    uint32_t p = pos + 2;                       // index of the next unread word (held in w)
+    uint32_t w = __ldg(d.words + p);
+    const int nk = d.nk;
+    pdl_wait();   // activations may come from the previous kernel of the stream
+    for (int k0 = 0; k0 < nk; k0 += kChunkK) {
+        const uintptr_t b = wbase + 2ull * p;
+        const uintptr_t a0 = b & ~uintptr_t(15);
+#pragma unroll 4
+        for (int c = 0; c < kWinBytes / 16; ++c) {
+            const uintptr_t src = a0 + 16ull * c;
+            if (src + 16 <= wend) {
+                cp_async16(win + 16u * c, reinterpret_cast<const void*>(src));
+            } else if (src < wend) {   // the buffer ends inside this chunk: word by word
+                for (uintptr_t q = src; q < wend; q += 2)
+                    *reinterpret_cast<uint16_t*>(wgen + 16u * c + (q - src)) =
+                        __ldg(reinterpret_cast<const uint16_t*>(q));
+            }
+        }
+        cp_async_commit();
+        cp_async_wait_all();
+        const uint32_t pw0 = win + static_cast<uint32_t>(b - a0);
+        uint32_t pw = pw0;
+        const int k1 = min(nk, k0 + kChunkK);
+        for (int k = k0; k < k1; ++k) {
+            float xv[1];
+            load_xs<1, 1, BF16X>(d, xcol, 1, k, xv);
+#pragma unroll
+            for (int r = 0; r < R; ++r) sym_step_ptx(st, w, pw, acc[0][r], xv[0], tb, magic);
+        }
+        p += (pw - pw0) >> 1;
+    }
+    if (st != kRansL) ++bad;
+}
+
 // Sets up a pass over tiles [t0, t0+kk) (consecutive), staging when possible,
 // and decodes it.  Streams j >= kk replay stream kk-1 with zero activation.
 template <int R, int K, int NACC, bool BF16X>
@@ -448,6 +505,14 @@ __device__ __forceinline__ void run_pass(const MatDev& d, const uint32_t*, uint1
         decode_pass<R, K, NACC, BF16X, true>(pos, xcol, kk, d, acc, bad);
         __syncwarp();   // stage is rewritten by the next pass
     } else {
+        const uint64_t limit = d.nwords >= 0 ? (uint64_t)d.nwords : (d.wlimit > 0 ? (uint64_t)d.wlimit : 0);
+        if constexpr (K == 1 && NACC == 1 && kStageBytes >= 32 * 32) {
+            if (limit > 0) {
+                decode_pass_windowed<R, BF16X>(pos[0], xcol, d, acc, bad, stage, lane, limit);
+                __syncwarp();   // stage is rewritten by the next pass
+                return;
+            }
+        }
         decode_pass<R, K, NACC, BF16X, false>(pos, xcol, kk, d, acc, bad);
     }
 }
