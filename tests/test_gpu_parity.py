@@ -275,8 +275,8 @@ def test_medium_launch_segments_rows(torch, rb):
 def test_tiles_larger_than_the_stage(torch, rb, rows, cols, R, C, bits):
     """Tiles whose words exceed the 8 KB per-warp stage decode through windows
     of each lane's stream: results match the oracle for the drop-in entry
-    (buffer length unknown), the bf16 entry (length known) and the step
-    launcher."""
+    (buffer length unknown), the bf16 entry (length known), the step launcher
+    and the decode to dense bf16."""
     codes = orc.synth_codes(rows, cols, bits, "gauss", seed=rows + C)
     rng = np.random.default_rng(cols)
     step = (0.01 * rng.uniform(0.5, 1.5, cols)).astype(np.float32)
@@ -291,3 +291,6 @@ def test_tiles_larger_than_the_stage(torch, rb, rows, cols, R, C, bits):
     rb.RansStep([m], [xb.cuda()], [y])()
     torch.cuda.synchronize()
     _check_y(y.cpu().numpy(), yref)
+    # decode to dense bf16 through the same windows, bit-exact
+    want = (torch.from_numpy(codes).float() * torch.from_numpy(step)).bfloat16()
+    assert torch.equal(m.decode().cpu(), want)

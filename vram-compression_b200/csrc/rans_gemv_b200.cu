@@ -434,12 +434,36 @@ __device__ __forceinline__ void decode_pass(const uint32_t (&pos)[K], const int 
 // staged symbol step (at most one word per symbol, so the reads stay inside
 // the window), and refills.  Copies stop at `limit` (words readable from
 // d.words); words beyond the stream's end are never consumed.
+constexpr int kWinBytes = kStageBytes / 32;   // per-lane window of a windowed pass
+constexpr int kWinWords = kWinBytes / 2;
+
+// Copies this lane's window: kWinBytes of d.words from the 16-byte boundary at
+// or below word p (that chunk holds word p, so it lies on a page the buffer
+// touches), nothing at or past byte `wend`.  Returns the shared address of
+// word p in the window.
+__device__ __forceinline__ uint32_t refill_window(const MatDev& d, uint8_t* wgen, uint32_t win, uint32_t p,
+                                                  uintptr_t wend) {
+    const uintptr_t b = reinterpret_cast<uintptr_t>(d.words) + 2ull * p;
+    const uintptr_t a0 = b & ~uintptr_t(15);
+#pragma unroll 4
+    for (int c = 0; c < kWinBytes / 16; ++c) {
+        const uintptr_t src = a0 + 16ull * c;
+        if (src + 16 <= wend) {
+            cp_async16(win + 16u * c, reinterpret_cast<const void*>(src));
+        } else if (src < wend) {   // the buffer ends inside this chunk: word by word
+            for (uintptr_t q = src; q < wend; q += 2)
+                *reinterpret_cast<uint16_t*>(wgen + 16u * c + (q - src)) = __ldg(reinterpret_cast<const uint16_t*>(q));
+        }
+    }
+    cp_async_commit();
+    cp_async_wait_all();
+    return win + static_cast<uint32_t>(b - a0);
+}
+
 template <int R, bool BF16X>
 __device__ __forceinline__ void decode_pass_windowed(uint32_t pos, const int (&xcol)[1], const MatDev& d,
                                                   float (&acc)[1][R], int& bad, uint16_t* stage, int lane,
                                                   uint64_t limit) {
-    constexpr int kWinBytes = kStageBytes / 32;
-    constexpr int kWinWords = kWinBytes / 2;
     constexpr int kChunkK = (kWinWords - 8) / R;   // head <= 7 words, then <= 1 word per symbol
     static_assert(kChunkK >= 1, "stage too small for windowed staging");
     const SmemMap sm = smem_map(0);
@@ -455,22 +479,7 @@ __device__ __forceinline__ void decode_pass_windowed(uint32_t pos, const int (&x
     const int nk = d.nk;
     pdl_wait();   // activations may come from the previous kernel of the stream
     for (int k0 = 0; k0 < nk; k0 += kChunkK) {
-        const uintptr_t b = wbase + 2ull * p;
-        const uintptr_t a0 = b & ~uintptr_t(15);
-#pragma unroll 4
-        for (int c = 0; c < kWinBytes / 16; ++c) {
-            const uintptr_t src = a0 + 16ull * c;
-            if (src + 16 <= wend) {
-                cp_async16(win + 16u * c, reinterpret_cast<const void*>(src));
-            } else if (src < wend) {   // the buffer ends inside this chunk: word by word
-                for (uintptr_t q = src; q < wend; q += 2)
-                    *reinterpret_cast<uint16_t*>(wgen + 16u * c + (q - src)) =
-                        __ldg(reinterpret_cast<const uint16_t*>(q));
-            }
-        }
-        cp_async_commit();
-        cp_async_wait_all();
-        const uint32_t pw0 = win + static_cast<uint32_t>(b - a0);
+        const uint32_t pw0 = refill_window(d, wgen, win, p, wend);
         uint32_t pw = pw0;
         const int k1 = min(nk, k0 + kChunkK);
         for (int k = k0; k < k1; ++k) {
@@ -828,6 +837,39 @@ __device__ __forceinline__ void decode_store(const MatDev& d, const uint32_t (&p
 // row-major matrix (the "decompress, then cuBLAS" comparator).  Same staging
 // and symbol step as the fused GEMV; each symbol becomes one 2-byte store,
 // coalesced across the warp (64 B per row segment).
+// decode_store for one tile whose words do not fit the stage: per-lane
+// windows as in decode_pass_windowed.
+template <int R>
+__device__ __forceinline__ void decode_store_windowed(const MatDev& d, uint32_t pos, __nv_bfloat16* orow,
+                                                      int col0, uint16_t* stage, int lane, uint64_t limit) {
+    constexpr int kChunkK = (kWinWords - 8) / R;
+    const SmemMap sm = smem_map(0);
+    const uint32_t magic = __shfl_sync(0xffffffffu, 0x4B000000u, 0);
+    uint8_t* const wgen = reinterpret_cast<uint8_t*>(stage) + lane * kWinBytes;
+    const uint32_t win = static_cast<uint32_t>(__cvta_generic_to_shared(wgen));
+    const uintptr_t wend = reinterpret_cast<uintptr_t>(d.words) + 2ull * limit;
+    uint32_t st = (static_cast<uint32_t>(__ldg(d.words + pos)) << 16) | __ldg(d.words + pos + 1);
+    uint32_t p = pos + 2;
+    uint32_t w = __ldg(d.words + p);
+    uint32_t roff[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) roff[r] = (uint32_t)r * (uint32_t)d.cols;
+    const int nk = d.nk;
+    for (int k0 = 0; k0 < nk; k0 += kChunkK) {
+        const uint32_t pw0 = refill_window(d, wgen, win, p, wend);
+        uint32_t pw = pw0;
+        const int k1 = min(nk, k0 + kChunkK);
+        for (int k = k0; k < k1; ++k) {
+            const float sv = __ldg(d.step + col0 + 32 * k) * kInvCodeScale;
+            __nv_bfloat16* o = orow + 32 * k;
+#pragma unroll
+            for (int r = 0; r < R; ++r)
+                o[roff[r]] = __float2bfloat16(sym_code(st, w, pw, sm.tab_s, sm.tab, true, d, magic) * sv);
+        }
+        p += (pw - pw0) >> 1;
+    }
+}
+
 template <int R, int K>
 __device__ __forceinline__ void decode_tiles(const MatDev& d, const SmemMap& sm, __nv_bfloat16* __restrict__ out,
                                              int64_t ntiles, int64_t t0, int lane) {
@@ -854,6 +896,13 @@ __device__ __forceinline__ void decode_tiles(const MatDev& d, const SmemMap& sm,
         for (int j = 0; j < K; ++j) pos[j] = soff + 2u * (pos[j] - w0 + head);
         decode_store<R, K, true>(d, pos, kk, orow, col0);
     } else {
+        if constexpr (K == 1 && kStageBytes >= 32 * 32) {
+            const uint64_t limit = d.nwords >= 0 ? (uint64_t)d.nwords : (d.wlimit > 0 ? (uint64_t)d.wlimit : 0);
+            if (limit > 0) {
+                decode_store_windowed<R>(d, pos[0], orow[0], col0[0], sm.stage, lane, limit);
+                return;
+            }
+        }
         decode_store<R, K, false>(d, pos, kk, orow, col0);
     }
 }
@@ -1178,7 +1227,8 @@ static int launch_decode_k(const MatDev& d, void* out, int k, cudaStream_t strea
     switch (k) {
         case 4: return launch_decode_t<R, 4>(d, out, stream);
         case 3: return launch_decode_t<R, 3>(d, out, stream);
-        default: return launch_decode_t<R, 2>(d, out, stream);
+        case 2: return launch_decode_t<R, 2>(d, out, stream);
+        default: return launch_decode_t<R, 1>(d, out, stream);
     }
 }
 
@@ -1193,10 +1243,10 @@ extern "C" int launch_rans_decode(int R, const void* words, const void* offs, co
     d.nrb = rows / R;
     d.nk = C / 32;
     d.tail_words = 2 + R * d.nk;
-    // tiles per warp pass: as many as the stage holds (2..4), while the
-    // matrix still gives two waves of warps; small matrices keep K = 2
+    // tiles per warp pass: as many as the stage holds (1..4), while the
+    // matrix still gives two waves of warps (small matrices: at most 2)
     const int64_t ntiles = (int64_t)d.nrb * d.ncb;
-    int64_t k = std::min<int64_t>(4, std::max<int64_t>(2, pass_symbols(d) / ((int64_t)R * C)));
+    int64_t k = std::min<int64_t>(4, std::max<int64_t>(1, pass_symbols(d) / ((int64_t)R * C)));
     while (k > 2 && ntiles / k < 2 * (int64_t)split_target()) --k;
     switch (R) {
         case 1: return launch_decode_k<1>(d, out, (int)k, stream);
