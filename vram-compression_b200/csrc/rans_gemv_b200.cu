@@ -307,7 +307,7 @@ __device__ __forceinline__ void load_xs(const MatDev& d, const int (&xcol)[K], i
 }
 
 #ifndef RB_INNER
-#define RB_INNER 1       // 0: C++ symbol step, 1: PTX symbol step, 2: PTX with mul.hi shifts
+#define RB_INNER 1       // 0: C++ symbol step, 1: PTX symbol step (staged passes)
 #endif
 #ifndef RB_XPREF
 #define RB_XPREF 0
@@ -466,6 +466,7 @@ __device__ __forceinline__ void decode_pass_windowed(uint32_t pos, const int (&x
                                                   uint64_t limit) {
     constexpr int kChunkK = (kWinWords - 8) / R;   // head <= 7 words, then <= 1 word per symbol
     static_assert(kChunkK >= 1, "stage too small for windowed staging");
+    static_assert(RB_LAYOUT == 1 && RB_ALIGNTAB, "windowed passes use the PTX symbol step");
     const SmemMap sm = smem_map(0);
     const uint32_t magic = __shfl_sync(0xffffffffu, 0x4B000000u, 0);
     const uint32_t tb = sm.tab_s;
@@ -843,6 +844,7 @@ template <int R>
 __device__ __forceinline__ void decode_store_windowed(const MatDev& d, uint32_t pos, __nv_bfloat16* orow,
                                                       int col0, uint16_t* stage, int lane, uint64_t limit) {
     constexpr int kChunkK = (kWinWords - 8) / R;
+    static_assert(RB_LAYOUT == 1 && RB_ALIGNTAB, "windowed passes use the PTX symbol step");
     const SmemMap sm = smem_map(0);
     const uint32_t magic = __shfl_sync(0xffffffffu, 0x4B000000u, 0);
     uint8_t* const wgen = reinterpret_cast<uint8_t*>(stage) + lane * kWinBytes;
