@@ -5,13 +5,14 @@
 //
 // Execution model (differs from the reference's one-stream-per-lane, one
 // global load per renormalisation, kernel/rans_gemv.cu:39-77):
-//   * a warp owns a WORK ITEM: in column mode (ncb > 1) a row block rb and a
-//     range of its column blocks, in row mode (ncb == 1) up to KROW row blocks.
-//     The item's tiles are consecutive in stream order, so their word streams
-//     form ONE contiguous span of `words`.
+//   * a warp owns a WORK ITEM: a row block rb and a range of its column
+//     blocks (a segment), decoded K tiles per pass.  The tiles of a pass are
+//     consecutive in stream order, so their word streams form ONE contiguous
+//     span of `words`.
 //   * the span is staged into a per-warp shared-memory buffer with 16-byte
 //     cp.async copies (fully coalesced), and every renormalisation word is then
-//     read from shared memory instead of global memory;
+//     read from shared memory instead of global memory (a one-tile pass too
+//     large for the buffer goes through per-lane windows of it);
 //   * each lane decodes K independent streams (lane l of K tiles) interleaved
 //     symbol by symbol, hiding the table-lookup -> multiply -> compare chain;
 //   * the 16 KB slot table is re-laid in shared memory (16 KB-aligned) as
@@ -62,10 +63,7 @@ constexpr int kPadWords = 8;
 #define RB_LAYOUT 1      // shared-memory table entry: 0 = sym|bias<<8|freq<<20, 1 = bias|sym<<12|freq<<20
 #endif
 #ifndef RB_I4_UNROLL
-#define RB_I4_UNROLL 2   // int4 baseline: column groups in flight per lane
-#endif
-#ifndef RB_I4_WAVES
-#define RB_I4_WAVES 2    // int4 baseline: rows per warp leave at least this many waves of warps
+#define RB_I4_UNROLL 4   // int4 baseline: column groups in flight per lane
 #endif
 #ifndef RB_ALIGNTAB
 #define RB_ALIGNTAB 1    // place the table at a 16 KB-aligned shared address (address = one LOP3)
@@ -941,46 +939,50 @@ __global__ void __launch_bounds__(256) int4_gemv_kernel(const uint32_t* __restri
                                                         const float4* __restrict__ x,
                                                         float* __restrict__ y, int rows, int cols) {
     const int lane = threadIdx.x & 31;
-    const int row0 = ((blockIdx.x * blockDim.x + threadIdx.x) >> 5) * kInt4Rows;
-    if (row0 >= rows) return;
     const int ngroup = cols / 8;
-    const uint32_t* wr[kInt4Rows];
-#pragma unroll
-    for (int r = 0; r < kInt4Rows; ++r)
-        wr[r] = w + (int64_t)min(row0 + r, rows - 1) * ngroup;   // rows past the end repeat the last
-    float acc[kInt4Rows];
-#pragma unroll
-    for (int r = 0; r < kInt4Rows; ++r) acc[r] = 0.f;
-    // per nibble position: scale of the activation, float offset, mask
+    // per nibble position: scale of the activation
     constexpr float kScale[8] = {1.f, 0.0625f, 0.00390625f, 0.000244140625f, 1.52587890625e-05f,
                                  1.f, 0.0625f, 0.00390625f};
+    const uint32_t magic = __shfl_sync(0xffffffffu, 0x4B000000u, 0);   // kept in a register
+    const int nwarps = (gridDim.x * blockDim.x) >> 5;
+    // grid-stride over groups of kInt4Rows rows: the grid holds only resident CTAs
+    for (int row0 = ((blockIdx.x * blockDim.x + threadIdx.x) >> 5) * kInt4Rows; row0 < rows;
+         row0 += nwarps * kInt4Rows) {
+        const uint32_t* wr[kInt4Rows];
+#pragma unroll
+        for (int r = 0; r < kInt4Rows; ++r)
+            wr[r] = w + (int64_t)min(row0 + r, rows - 1) * ngroup;   // rows past the end repeat the last
+        float acc[kInt4Rows];
+#pragma unroll
+        for (int r = 0; r < kInt4Rows; ++r) acc[r] = 0.f;
 #pragma unroll kI4Unroll
-    for (int g = lane; g < ngroup; g += 32) {
-        const float4 x0 = __ldg(x + 2 * g);
-        const float4 x1 = __ldg(x + 2 * g + 1);
-        const float xv[8] = {x0.x * kScale[0], x0.y * kScale[1], x0.z * kScale[2], x0.w * kScale[3],
-                             x1.x * kScale[4], x1.y * kScale[5], x1.z * kScale[6], x1.w * kScale[7]};
-        uint32_t q[kInt4Rows];
+        for (int g = lane; g < ngroup; g += 32) {
+            const float4 x0 = __ldg(x + 2 * g);
+            const float4 x1 = __ldg(x + 2 * g + 1);
+            const float xv[8] = {x0.x * kScale[0], x0.y * kScale[1], x0.z * kScale[2], x0.w * kScale[3],
+                                 x1.x * kScale[4], x1.y * kScale[5], x1.z * kScale[6], x1.w * kScale[7]};
+            uint32_t q[kInt4Rows];
 #pragma unroll
-        for (int r = 0; r < kInt4Rows; ++r) q[r] = __ldg(wr[r] + g);
+            for (int r = 0; r < kInt4Rows; ++r) q[r] = __ldg(wr[r] + g);
 #pragma unroll
-        for (int r = 0; r < kInt4Rows; ++r) {
-            const uint32_t qh = q[r] >> 20;
+            for (int r = 0; r < kInt4Rows; ++r) {
+                const uint32_t qh = q[r] >> 20;
 #pragma unroll
-            for (int b = 0; b < 8; ++b) {
-                const int s = b < 5 ? b : b - 5;
-                const uint32_t src = b < 5 ? q[r] : qh;
-                const uint32_t bits = (src & (0xFu << (4 * s))) | 0x4B000000u;
-                const float off = 8388608.0f + 8.0f * static_cast<float>(1u << (4 * s));
-                const float c = __int_as_float(bits) - off;
-                acc[r] = fmaf(c, xv[b], acc[r]);
+                for (int b = 0; b < 8; ++b) {
+                    const int sh = b < 5 ? b : b - 5;
+                    const uint32_t src = b < 5 ? q[r] : qh;
+                    uint32_t bits;   // (src & 0xF << 4sh) | magic: one LOP3
+                    asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(bits) : "r"(src), "r"(0xFu << (4 * sh)), "r"(magic));
+                    const float off = 8388608.0f + 8.0f * static_cast<float>(1u << (4 * sh));
+                    acc[r] = fmaf(__int_as_float(bits) - off, xv[b], acc[r]);
+                }
             }
         }
+        const float s = reduce_scatter<kInt4Rows>(acc, lane);
+        constexpr int kShift = 5 - Log2<kInt4Rows>::value;
+        const int r = lane >> kShift;
+        if ((lane & ((1 << kShift) - 1)) == 0 && row0 + r < rows) y[row0 + r] = s;
     }
-    const float s = reduce_scatter<kInt4Rows>(acc, lane);
-    constexpr int kShift = 5 - Log2<kInt4Rows>::value;
-    const int r = lane >> kShift;
-    if ((lane & ((1 << kShift) - 1)) == 0 && row0 + r < rows) y[row0 + r] = s;
 }
 
 // ------------------------------------------------------------ host side
@@ -1073,6 +1075,22 @@ static bool set_smem_attr(const void* fn, unsigned long long* done_mask) {
         return false;
     __atomic_fetch_or(done_mask, bit, __ATOMIC_ACQ_REL);
     return true;
+}
+
+// CTAs of `fn` (threads per CTA, dynamic shared bytes) resident at once on
+// the current device; cached per device in `cache` (0 = not yet asked).
+static int resident_blocks_any(const void* fn, int threads, size_t smem, int* cache) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 1;
+    int* slot = &cache[dev & 63];
+    int v = __atomic_load_n(slot, __ATOMIC_ACQUIRE);
+    if (v > 0) return v;
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, threads, smem) != cudaSuccess || per_sm < 1)
+        per_sm = 1;
+    v = per_sm * sm_count();
+    __atomic_store_n(slot, v, __ATOMIC_RELEASE);
+    return v;
 }
 
 // CTAs of `fn` (kThreads threads, kSmemBytes shared) resident at once on the
@@ -1264,17 +1282,21 @@ extern "C" int launch_int4_gemv(const void* w, const void* x, void* y, int rows,
                                 cudaStream_t stream) {
     if (rows <= 0 || cols <= 0 || cols % 32) return -2;
     const int threads = 256;
-    // rows per warp: the most that still leaves RB_I4_WAVES waves of warps
-    // (memory latency needs them), else one
-    const int64_t want = RB_I4_WAVES * split_target();
-    const int rw = rows / 8 >= want ? 8 : rows / 4 >= want ? 4 : rows / 2 >= want ? 2 : 1;
+    // rows per warp: 4 (each activation load serves 4 rows) while that still
+    // keeps a quarter of the resident warps busy, else 2, else 1 (few rows,
+    // many columns).  Measured on the BASELINE shapes: 8 rows per warp or
+    // one-row warps on tall matrices are up to 1.8x slower.
+    static int resident[64] = {};
+    const int64_t slots = (int64_t)resident_blocks_any((const void*)int4_gemv_kernel<4>, threads, 0, resident) *
+                          (threads / 32);
+    int rw = rows / 4 >= slots / 4 ? 4 : rows / 2 >= slots / 4 ? 2 : 1;
     const int64_t warps = (rows + rw - 1) / rw;
-    const int grid = (int)((warps * 32 + threads - 1) / threads);
+    const int64_t blocks = (warps * 32 + threads - 1) / threads;
+    const int grid = (int)std::min<int64_t>(blocks, std::max<int64_t>(1, slots / (threads / 32)));
     const uint32_t* wq = static_cast<const uint32_t*>(w);
     const float4* xv = static_cast<const float4*>(x);
     float* yv = static_cast<float*>(y);
     switch (rw) {
-        case 8: int4_gemv_kernel<8><<<grid, threads, 0, stream>>>(wq, xv, yv, rows, cols); break;
         case 4: int4_gemv_kernel<4><<<grid, threads, 0, stream>>>(wq, xv, yv, rows, cols); break;
         case 2: int4_gemv_kernel<2><<<grid, threads, 0, stream>>>(wq, xv, yv, rows, cols); break;
         default: int4_gemv_kernel<1><<<grid, threads, 0, stream>>>(wq, xv, yv, rows, cols); break;
