@@ -549,6 +549,7 @@ def main():
             "compressed_gbs": round(compressed_gbs_step, 2),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": traffic, "peak_kind": peak_kind,
+                         "frac_of_nominal_7700_gbs": round(achieved / 7700.0, 4),
                          "kernel": "gemv_step_kernel", "kernel_ms": round(k_ms, 4)},
             "tsymbols_per_s": round(weights_step / (t_ms * 1e-3) / 1e12, 4),
             "gpu_launches": args.steps * step.kernels,
