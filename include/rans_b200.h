@@ -133,15 +133,20 @@ int rans_gemv_step_kernels(const void* workspace);
  * loop that forbids allocation after start-up, a runtime without an allocator
  * handle to hand over.  It plans and launches in one call and allocates
  * nothing: the plan goes to a 256 KB file-scope device array that every GPU
- * loading this library holds until exit.  `descs` is a HOST array of device
- * pointers, as for rans_gemv_step_plan.  Returns -3 when the plan of these
- * descriptors exceeds 256 KB (about 14,000 eight-warp chunks, e.g. one
- * Qwen2.5-1.5B decoder step; split larger steps into several calls).
+ * loading this library holds until exit, uploaded through kernel launch
+ * parameters (no host buffer is read after the call returns).  `descs` is a
+ * HOST array of device pointers, as for rans_gemv_step_plan.  The plan is the
+ * simple one (whole row blocks per warp), without the split planning of
+ * rans_gemv_step_plan: same results, slower small launches.
+ * Plan bytes = 32 + 200*n + 16 * sum_i ceil(rows_i / (8*R)); above 256 KB it
+ * returns -3 before any GPU work.  At R = 8 a whole 28-layer Qwen2.5-1.5B step
+ * (196 matrices, 10,080 chunks) takes about 200 KB; at R = 1 one layer takes
+ * about 47 KB, so split such a step into calls of at most five layers.
  * The first call on a device looks up the array's device address with that
  * device current; make that first call before any stream capture.  All calls
- * share the one array and it keeps the last call's plan: calls whose work
- * overlaps on the GPU (different streams, or graphs replaying one call while
- * another plans) race.  No counterpart in the reference. */
+ * share the one array, which keeps the last call's plan: calls whose work
+ * overlaps on the GPU (for example on different streams) race.  No
+ * counterpart in the reference. */
 int rans_gemv_step_noalloc(const RansGemvDesc* descs, int n, int R, cudaStream_t stream);
 
 /* ------------------------------------------------------------ host encoder

@@ -1,9 +1,8 @@
 """Generate the golden fixtures in this folder from the REFERENCE implementation.
 
-Run once in a container where the reference tree is mounted (default
-/root/reference, override with $RANS_REFERENCE):
+Run once where the reference checkout is available, naming it (required):
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py <path to the reference checkout>
 
 It imports the reference's own kernel/rans.py (encoder, table, reference
 decoder) and kernel/bench.py (synthetic code generator) unchanged and records
@@ -28,7 +27,9 @@ import sys
 
 import numpy as np
 
-REF = os.environ.get("RANS_REFERENCE", "/root/reference")
+if len(sys.argv) != 2 or not os.path.isfile(os.path.join(sys.argv[1], "kernel", "rans.py")):
+    sys.exit("usage: make_golden.py <path to the reference checkout (holding kernel/rans.py)>")
+REF = os.path.abspath(sys.argv[1])
 sys.path.insert(0, os.path.join(REF, "kernel"))
 import rans  # noqa: E402  (the reference's kernel/rans.py)
 import bench  # noqa: E402  (the reference's kernel/bench.py)

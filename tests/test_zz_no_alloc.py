@@ -31,7 +31,8 @@ def _lib():
 
 def test_noalloc_rejects_oversize_plan():
     rb, lib = _lib()
-    # 2^20 rows at R=1 -> 262,144 row-mode items -> 32,768 chunks: over 256 KB.
+    # 2^20 rows at R=1 -> 2^20 row blocks, one item each -> 131,072 eight-item
+    # chunks -> a plan of about 2 MB: over the 256 KB array.
     d = rb.RansGemvDesc(None, None, None, None, None, None, -1, 1 << 20, 64, 64, 0)
     arr = (rb.RansGemvDesc * 1)(d)
     assert lib.rans_gemv_step_noalloc(ctypes.addressof(arr), 1, 1, None) == -3

@@ -1675,17 +1675,43 @@ extern "C" int rans_gemv_step_launch(int R, const void* workspace, int grid, cud
 // private cudaMalloc behind its back fragments it, or fails under memory
 // pressure), an inference loop that forbids allocation after start-up to keep
 // its latency predictable, or a runtime with no allocator handle to give us.
-// rans_gemv_step_noalloc serves them: the work plan that rans_gemv_step_plan
-// writes into a caller-allocated workspace lives here in a fixed-size
-// file-scope device array instead.
+// rans_gemv_step_noalloc serves them: its work plan lives in a fixed-size
+// file-scope device array instead of a caller-allocated workspace.  The plan
+// is the simple one (whole row blocks per warp, eight warps per CTA, longest
+// chunks first): it needs no segment partials, counters or prescaled
+// activations, so the array holds nothing but descriptors and chunks.  The
+// latency-bound split plans of rans_gemv_step_plan are not used here; results
+// are the same, small launches run slower.
+// Plan bytes = 32 + 200 * n + 16 * sum over matrices of ceil(rows / (8 R)).
+static_assert(sizeof(StepHeader) == 32 && sizeof(MatDev) == 200 && sizeof(Chunk) == 16,
+              "the plan-size formula of rans_gemv_step_noalloc (include/rans_b200.h)");
 constexpr size_t kNoAllocScratchBytes = 256 * 1024;   // the plan's maximum size
 constexpr int kNoAllocMaxDevices = 64;
 
 static __device__ __align__(256) uint8_t g_step_scratch[kNoAllocScratchBytes];
 
-// Host staging of the plan (static: no heap) and, per device, the device
-// address of g_step_scratch (the host-side name is only a stand-in).
+// The plan reaches the device inside kernel launch parameters, a piece of at
+// most kPlanPieceBytes per launch (the parameter space of a launch is 32,764
+// bytes on sm_70 and later with CUDA 12.1+).  A launch copies its parameters
+// when it is issued, so nothing on the host has to outlive the call: no
+// pageable or pinned staging buffer is read later by the device.
+constexpr int kPlanPieceBytes = 32000;
+struct PlanPiece {
+    uint32_t offset, nbytes;             // destination offset in g_step_scratch, bytes (multiple of 16)
+    uint4 bytes[kPlanPieceBytes / 16];
+};
+static_assert(sizeof(PlanPiece) <= 32764, "plan piece exceeds the kernel parameter space");
+
+__global__ void __launch_bounds__(256) write_plan_kernel(const __grid_constant__ PlanPiece piece) {
+    uint4* dst = reinterpret_cast<uint4*>(g_step_scratch + piece.offset);
+    for (uint32_t i = threadIdx.x; i < piece.nbytes / 16; i += blockDim.x) dst[i] = piece.bytes[i];
+}
+
+// Host staging of the plan (static: no heap), the parameter block of one
+// piece, and, per device, the device address of g_step_scratch (the
+// host-side name is only a stand-in).
 static uint8_t g_noalloc_host[kNoAllocScratchBytes];
+static PlanPiece g_noalloc_piece;
 static void* g_noalloc_dev[kNoAllocMaxDevices];
 static std::mutex g_noalloc_mu;
 
@@ -1748,10 +1774,18 @@ extern "C" int rans_gemv_step_noalloc(const RansGemvDesc* descs, int n, int R, c
         if (a.desc != b.desc) return a.desc < b.desc;
         return a.item0 < b.item0;
     });
-    // A pageable-source copy returns once the bytes are staged, so the static
-    // host buffer may be rewritten by the next call.
-    e = cudaMemcpyAsync(g_noalloc_dev[dev], g_noalloc_host, bytes, cudaMemcpyHostToDevice, stream);
-    if (e != cudaSuccess) return (int)e;
+    // Upload through launch parameters, piece by piece, in stream order before
+    // the step kernel that reads the plan.
+    const size_t padded = (bytes + 15) & ~size_t(15);
+    for (size_t off = 0; off < padded; off += kPlanPieceBytes) {
+        const size_t nb = std::min<size_t>(kPlanPieceBytes, padded - off);
+        g_noalloc_piece.offset = (uint32_t)off;
+        g_noalloc_piece.nbytes = (uint32_t)nb;
+        std::memcpy(g_noalloc_piece.bytes, g_noalloc_host + off, nb);
+        write_plan_kernel<<<1, 256, 0, stream>>>(g_noalloc_piece);
+        e = cudaGetLastError();
+        if (e != cudaSuccess) return (int)e;
+    }
     return rans_gemv_step_launch(R, g_noalloc_dev[dev], (int)nchunks, stream);
 }
 

@@ -153,6 +153,11 @@ class ShardedStep:
         return self.step.kernels
 
     def __call__(self):
+        if self.exchange == "fused":
+            # The kernel stores into every rank's full outputs: first make sure
+            # no rank still reads the previous call's result (back-to-back
+            # calls would otherwise overwrite it under a slower rank).
+            self.hdl.barrier(channel=1, timeout_ms=self.timeout_ms)
         self.step()
         if self.exchange == "fused":
             # every rank's rows are in every rank's buffer once all ranks have
