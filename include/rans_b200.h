@@ -36,7 +36,7 @@ extern "C" {
 typedef struct CUstream_st* cudaStream_t;
 #endif
 
-#define RANS_B200_ABI_VERSION 2   /* 2: escape-code entry points, rans_gemv_step_kernels */
+#define RANS_B200_ABI_VERSION 3   /* 2: escape-code entry points, rans_gemv_step_kernels; 3: chain launcher */
 
 /* ---------------------------------------------------------------- drop-in
  * The three entry points of the reference library, same names, argument
@@ -126,6 +126,59 @@ int rans_gemv_step_plan_peers(const RansGemvDesc* descs, const void* const* peer
  * (kernel/bench.py:104-107, kernel/rans.py:147-151). */
 int rans_gemv_step_launch(int R, const void* workspace, int grid, cudaStream_t stream);
 int rans_gemv_step_kernels(const void* workspace);
+
+/* ------------------------------------------------------------ chain launcher
+ * A decoder step as a chain of dependent phases (per layer {q,k,v} -> o ->
+ * {gate,up} -> down: phase p+1 reads what phase p wrote), run from ONE
+ * persistent grid.  phase[i] (0..P-1, every phase non-empty) is descriptor
+ * i's phase; chunks of phase p start only after every chunk of phase p-1 has
+ * finished (and, with `sync`, after every rank has signalled phase p-1).  The
+ * table load and an L2 warm-up of the weights of a waiting chunk overlap the
+ * previous phase.  Activations are read through L2, so phase p+1's x may be
+ * phase p's y (the fp32 pre-scaled convention: step NULL) or a buffer written
+ * by an earlier kernel.  No counterpart in the reference, whose harness
+ * launches one kernel per matrix (kernel/bench.py:104-107,
+ * kernel/rans.py:147-151); this is the layer-level launcher of its survey.   */
+
+/* Row-sharded chain over the GPUs of one node (one process per GPU).
+ * arrive: this rank's uint32[P] arrival counters in memory every rank can
+ * write (NVLink peer mapping / symmetric memory); arrive_peer[r]: the address,
+ * valid on this GPU, of rank r's counters (this rank included); peer_y as for
+ * rans_gemv_step_plan_peers.  Every rank plans (which zeroes its counters),
+ * then all ranks pass a host barrier, then every rank launches the same number
+ * of times.  A phase's output rows are stored into every rank's buffer, and
+ * the phase is complete on a rank once all ranks have added 1 to its counter
+ * there.  A faster rank may already run the next launch's first phase while
+ * a slower one runs this launch's last, so phase 0's outputs must not be
+ * read by the last phase. */
+typedef struct RansChainSync {
+    int32_t nranks;                  /* <= 8 */
+    int32_t rank;
+    void* arrive;
+    void* const* arrive_peer;        /* [nranks] */
+    const void* const* peer_y;       /* [n * nranks] */
+} RansChainSync;
+
+/* Device workspace bytes for this chain; -1 bad R, -2 bad shape or phases. */
+int64_t rans_gemv_chain_workspace_bytes(const RansGemvDesc* descs, const int* phase, int n, int R);
+
+/* Plan the chain into `workspace` (HOST arrays descs, phase; sync NULL on one
+ * GPU).  timeout_ms bounds every dependency wait of the kernel.  Returns the
+ * launch grid (the CTAs resident at once, at most the number of chunks) in
+ * *grid_out.  Synchronises `stream`; -3 when workspace_bytes is too small. */
+int rans_gemv_chain_plan(const RansGemvDesc* descs, const int* phase, int n, int R,
+                         const RansChainSync* sync, int timeout_ms, void* workspace,
+                         size_t workspace_bytes, int* grid_out, cudaStream_t stream);
+
+/* One launch of a planned chain (one kernel). */
+int rans_gemv_chain_launch(int R, const void* workspace, int grid, cudaStream_t stream);
+
+/* Synchronises `stream` and reports the chain's state: 0 when every wait of
+ * the launches so far ended in time, -5 when one ran out (*phase_out = the
+ * phase it waited for; outputs of that launch are incomplete).  Reading -5
+ * clears it; until then launches return at once without work.  A multi-GPU
+ * chain must then be planned again on every rank. */
+int rans_gemv_chain_status(void* workspace, int* phase_out, cudaStream_t stream);
 
 /* The same decoder step for callers that cannot allocate device memory when
  * they run it: a framework whose caching allocator owns the whole pool (a

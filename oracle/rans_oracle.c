@@ -5,6 +5,7 @@
  * of bench.py.  Never linked into the product library.
  *
  *   oracle_build_table   kernel/rans.py:34-51   (12-bit static table)
+ *   oracle_encode        kernel/rans.py:55-98   (lane order + encoder)
  *   oracle_decode        kernel/rans.py:101-123 (decoder, final-state check)
  *   oracle_decode_gemv   kernel/rans.py:101-123 + kernel/bench.py:52-56
  *                        (decode, then dot with the step-folded activation)
@@ -13,6 +14,7 @@
  * at row rb*R + r and column cb*C + lane + 32k (kernel/rans.py:55-59).
  */
 #include <math.h>
+#include <stdlib.h>
 #include <stdint.h>
 #include <string.h>
 
@@ -149,4 +151,75 @@ int64_t oracle_decode_gemv(const uint16_t* words, const uint32_t* offs, const ui
     }
     (void)rows;
     return bad;
+}
+
+/* Symbol i (0..n-1) of stream s in stream order: for k < C/32, for r < R, the
+ * code at row rb*R + r, column cb*C + lane + 32k (kernel/rans.py:55-59). */
+static inline uint8_t stream_sym(const int8_t* codes, int cols, int R, int C, int64_t s, int i) {
+    const int ncb = cols / C;
+    const int64_t tile = s / 32;
+    const int lane = (int)(s % 32);
+    const int64_t rb = tile / ncb, cb = tile % ncb;
+    const int k = i / R, r = i % R;
+    return (uint8_t)((int)codes[(rb * R + r) * (int64_t)cols + cb * C + lane + 32 * k] + SYM_OFFSET);
+}
+
+/* Encodes stream s (kernel/rans.py:70-91): symbols pushed last to first from
+ * state RANS_L; before a push the state emits its low 16 bits while
+ * state >= freq << 20.  With out == NULL only counts the emitted words;
+ * otherwise writes [state >> 16, state & 0xffff, emitted words reversed]. */
+static int encode_one(const int8_t* codes, int cols, int R, int C, int64_t s, const int64_t* freq,
+                      const int64_t* cum, int nemit_known, uint16_t* out) {
+    const int n = (C / 32) * R;
+    uint64_t x = RANS_L;
+    int nemit = 0;
+    for (int i = n - 1; i >= 0; --i) {
+        const uint8_t sym = stream_sym(codes, cols, R, C, s, i);
+        const uint64_t f = (uint64_t)freq[sym], c = (uint64_t)cum[sym];
+        if (x >= (f << 20)) {
+            if (out) out[2 + nemit_known - 1 - nemit] = (uint16_t)(x & 0xFFFFu);
+            ++nemit;
+            x >>= 16;
+        }
+        x = ((x / f) << SCALE_BITS) + x % f + c;
+    }
+    if (out) {
+        out[0] = (uint16_t)(x >> 16);
+        out[1] = (uint16_t)(x & 0xFFFFu);
+    }
+    return nemit;
+}
+
+/* Encode int8 codes (rows x cols, row-major) with the table's freq/cum into
+ * words (+8 zero pad words) and offs; two passes over the streams (count,
+ * then write), OpenMP over streams.  Returns 0, -3 when words_cap is too
+ * small. */
+int oracle_encode(const int8_t* codes, int rows, int cols, int R, int C, const int64_t* freq,
+                  const int64_t* cum, uint16_t* words, int64_t words_cap, uint32_t* offs,
+                  int64_t* nwords_out, int threads) {
+    const int64_t nstreams = (int64_t)rows * cols * 32 / ((int64_t)R * C);
+    int* nemit = (int*)malloc(sizeof(int) * (size_t)(nstreams > 0 ? nstreams : 1));
+    if (!nemit) return -3;
+#ifdef _OPENMP
+#pragma omp parallel for schedule(static) num_threads(threads > 0 ? threads : 1)
+#endif
+    for (int64_t s = 0; s < nstreams; ++s) nemit[s] = encode_one(codes, cols, R, C, s, freq, cum, 0, NULL);
+    int64_t total = 0;
+    for (int64_t s = 0; s < nstreams; ++s) {
+        offs[s] = (uint32_t)total;
+        total += nemit[s] + 2;
+    }
+    if (total + 8 > words_cap) {
+        free(nemit);
+        return -3;
+    }
+#ifdef _OPENMP
+#pragma omp parallel for schedule(static) num_threads(threads > 0 ? threads : 1)
+#endif
+    for (int64_t s = 0; s < nstreams; ++s)
+        encode_one(codes, cols, R, C, s, freq, cum, nemit[s], words + offs[s]);
+    memset(words + total, 0, 8 * sizeof(uint16_t));
+    *nwords_out = total + 8;
+    free(nemit);
+    return 0;
 }

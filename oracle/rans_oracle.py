@@ -9,6 +9,7 @@ snuri00/vram-compression:
   * ``build_table``   follows kernel/rans.py:34-51   (12-bit static table)
   * ``lane_order``    follows kernel/rans.py:55-59   (tile/lane interleave)
   * ``encode``        follows kernel/rans.py:62-98   (32-bit state rANS encoder)
+  * ``c_encode``      the same encoder in C (rans_oracle.c, OpenMP), for large shapes
   * ``decode``        follows kernel/rans.py:101-123 (reference decoder) and the
                       device step of kernel/rans_gemv.cu:32-37
   * ``synth_codes``   follows kernel/bench.py:26-35  (synthetic ECSQ codes)
@@ -267,6 +268,8 @@ def c_lib():
         lib.oracle_decode_gemv.restype = i64
         lib.oracle_build_table.argtypes = [vp, i64, vp, vp, vp]
         lib.oracle_build_table.restype = i32
+        lib.oracle_encode.argtypes = [vp, i32, i32, i32, i32, vp, vp, vp, i64, vp, vp, i32]
+        lib.oracle_encode.restype = i32
         _LIB = lib
     return _LIB
 
@@ -331,3 +334,36 @@ def c_build_table(sym: np.ndarray):
     if rc != 0:
         raise ValueError("degenerate distribution (single symbol)")
     return freq, cum, table
+
+
+def c_encode(codes: np.ndarray, R: int, C: int, threads: int = 1) -> dict:
+    """encode() in C (kernel/rans.py:34-98): same dict, same bytes; OpenMP over
+    streams.  For the large shapes of the CPU baseline and bench checks."""
+    lib = c_lib()
+    codes = np.asarray(codes)
+    rows, cols = codes.shape
+    check_tiling(rows, cols, R, C)
+    sym = codes_to_symbols(codes)
+    freq, cum, table = c_build_table(sym)
+    c8 = np.ascontiguousarray((sym.astype(np.int16) - SYM_OFFSET).astype(np.int8))
+    nstream = rows * cols * 32 // (R * C)
+    n = (C // 32) * R
+    cap = nstream * (n + 2) + PAD_WORDS
+    words = np.empty(cap, np.uint16)
+    offs = np.empty(nstream, np.uint32)
+    nw = ctypes.c_int64(0)
+    rc = lib.oracle_encode(c8.ctypes.data, rows, cols, R, C, freq.ctypes.data, cum.ctypes.data,
+                           words.ctypes.data, cap, offs.ctypes.data, ctypes.byref(nw), threads)
+    if rc != 0:
+        raise RuntimeError(f"oracle_encode failed ({rc})")
+    words = words[: nw.value].copy()
+    lens_total = nw.value - PAD_WORDS
+    nweights = codes.size
+    hist = np.bincount(sym.ravel(), minlength=256)
+    present = hist > 0
+    p = freq[present].astype(np.float64) / PROB_M
+    return dict(words=words, offs=offs, table=table, R=R, C=C, shape=tuple(codes.shape),
+                bits_payload=16 * (lens_total - 2 * nstream) / nweights,
+                bits_state_offs=64 * nstream / nweights,
+                bits_table=32 * PROB_M / nweights,
+                entropy_model=float(-(hist[present] * np.log2(p)).sum() / nweights))

@@ -30,6 +30,19 @@ def test_encode_matches_reference(path):
 
 
 @pytest.mark.parametrize("path", CASES, ids=IDS)
+def test_c_encoder_matches_reference(path):
+    """The C restatement of the encoder (used for large shapes by bench.py's
+    CPU legs and checks) writes the reference's bytes."""
+    codes, enc, *_ , bits = load_case(path)
+    mine = orc.c_encode(codes, enc["R"], enc["C"], threads=3)
+    assert np.array_equal(mine["table"], enc["table"])
+    assert np.array_equal(mine["offs"], enc["offs"])
+    assert np.array_equal(mine["words"], enc["words"])
+    np.testing.assert_allclose([mine["bits_payload"], mine["bits_state_offs"], mine["bits_table"],
+                                mine["entropy_model"]], bits, rtol=0, atol=1e-12)
+
+
+@pytest.mark.parametrize("path", CASES, ids=IDS)
 def test_decoders_match_reference(path):
     codes, enc, step, x, y, _ = load_case(path)
     assert np.array_equal(orc.decode(enc), codes)
@@ -59,6 +72,7 @@ def test_config1_digests():
     assert sha(codes.astype(np.int32)) == meta["sha_codes"]
     enc = orc.encode(codes, meta["R"], meta["C"])
     assert sha(enc["words"]) == meta["sha_words"]
+    assert sha(orc.c_encode(codes, meta["R"], meta["C"], threads=4)["words"]) == meta["sha_words"]
     assert sha(enc["offs"]) == meta["sha_offs"]
     assert sha(enc["table"]) == meta["sha_table"]
     assert np.array_equal(orc.c_decode_codes(enc), codes)

@@ -27,6 +27,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <algorithm>
+#include <cstddef>
 #include <mutex>
 #include <unordered_map>
 #include <vector>
@@ -106,8 +107,9 @@ struct MatDev {
     uint32_t* counters;    // [nrb] arrivals per row block, zero between launches (workspace)
 };
 
-struct Chunk {             // one CTA of the step launcher
-    int desc, item0, nitems, pad_;
+struct Chunk {             // one CTA's share of work: items [item0, item0 + nitems) of one matrix
+    int desc, item0, nitems;
+    int phase;             // chain launcher: dependency phase of the matrix (0 for a step plan)
 };
 
 struct StepHeader {
@@ -187,13 +189,23 @@ __device__ __forceinline__ float entry_code(uint32_t e) {
 #endif
 }
 
-template <bool BF16X>
+// Activation load mode XM: bit 0 set = bf16 x times the fp32 step (folded
+// here), clear = fp32 x already multiplied by the step; bit 1 set = load x
+// through L2 only (ld.global.cg), for kernels in which x may have been written
+// by other CTAs earlier in the same launch (the chain kernel: a phase's input
+// is an earlier phase's output), where the non-coherent path could return a
+// stale line.
+constexpr int kXBf16 = 1, kXCoherent = 2;
+
+template <int XM>
 __device__ __forceinline__ float load_x(const MatDev& d, int c) {
-    if (BF16X) {
-        const __nv_bfloat16* xb = reinterpret_cast<const __nv_bfloat16*>(d.x);
-        return __bfloat162float(xb[c]) * __ldg(d.step + c);
+    if (XM & kXBf16) {
+        const unsigned short* xb = reinterpret_cast<const unsigned short*>(d.x);
+        const unsigned short v = (XM & kXCoherent) ? __ldcg(xb + c) : xb[c];
+        return __uint_as_float((uint32_t)v << 16) * __ldg(d.step + c);   // bf16 -> fp32 is exact
     } else {
-        return __ldg(reinterpret_cast<const float*>(d.x) + c);
+        const float* xf = reinterpret_cast<const float*>(d.x);
+        return (XM & kXCoherent) ? __ldcg(xf + c) : __ldg(xf + c);
     }
 }
 
@@ -292,15 +304,15 @@ struct WordSrc<false> {
     __device__ __forceinline__ static uint32_t at(const MatDev& d, uint32_t p) { return __ldg(d.words + p); }
 };
 
-template <int K, int NACC, bool BF16X>
+template <int K, int NACC, int XM>
 __device__ __forceinline__ void load_xs(const MatDev& d, const int (&xcol)[K], int kk, int k, float (&xv)[K]) {
     if (NACC == K) {
-        const float v = load_x<BF16X>(d, xcol[0] + 32 * k);
+        const float v = load_x<XM>(d, xcol[0] + 32 * k);
 #pragma unroll
         for (int j = 0; j < K; ++j) xv[j] = v;
     } else {
 #pragma unroll
-        for (int j = 0; j < K; ++j) xv[j] = (j < kk) ? load_x<BF16X>(d, xcol[j] + 32 * k) : 0.f;
+        for (int j = 0; j < K; ++j) xv[j] = (j < kk) ? load_x<XM>(d, xcol[j] + 32 * k) : 0.f;
     }
 }
 
@@ -368,7 +380,7 @@ __device__ __forceinline__ void sym_step_ptx(uint32_t& st, uint32_t& w, uint32_t
 #endif
 }
 
-template <int R, int K, int NACC, bool BF16X, bool STAGED>
+template <int R, int K, int NACC, int XM, bool STAGED>
 __device__ __forceinline__ void decode_pass(const uint32_t (&pos)[K], const int (&xcol)[K], int kk,
                                             const MatDev& d, float (&acc)[NACC][R], int& bad) {
     using W = WordSrc<STAGED>;
@@ -390,15 +402,15 @@ __device__ __forceinline__ void decode_pass(const uint32_t (&pos)[K], const int 
     const int nk = d.nk;
     pdl_wait();   // activations may come from the previous kernel of the stream
     float xn[K];
-    if (RB_XPREF) load_xs<K, NACC, BF16X>(d, xcol, kk, 0, xn);
+    if (RB_XPREF) load_xs<K, NACC, XM>(d, xcol, kk, 0, xn);
     for (int k = 0; k < nk; ++k) {
         float xv[K];
         if (RB_XPREF) {
 #pragma unroll
             for (int j = 0; j < K; ++j) xv[j] = xn[j];
-            if (k + 1 < nk) load_xs<K, NACC, BF16X>(d, xcol, kk, k + 1, xn);   // prefetch next k-step
+            if (k + 1 < nk) load_xs<K, NACC, XM>(d, xcol, kk, k + 1, xn);   // prefetch next k-step
         } else {
-            load_xs<K, NACC, BF16X>(d, xcol, kk, k, xv);
+            load_xs<K, NACC, XM>(d, xcol, kk, k, xv);
         }
 #pragma unroll
         for (int r = 0; r < R; ++r) {
@@ -458,7 +470,7 @@ __device__ __forceinline__ uint32_t refill_window(const MatDev& d, uint8_t* wgen
     return win + static_cast<uint32_t>(b - a0);
 }
 
-template <int R, bool BF16X>
+template <int R, int XM>
 __device__ __forceinline__ void decode_pass_windowed(uint32_t pos, const int (&xcol)[1], const MatDev& d,
                                                   float (&acc)[1][R], int& bad, uint16_t* stage, int lane,
                                                   uint64_t limit) {
@@ -483,7 +495,7 @@ __device__ __forceinline__ void decode_pass_windowed(uint32_t pos, const int (&x
         const int k1 = min(nk, k0 + kChunkK);
         for (int k = k0; k < k1; ++k) {
             float xv[1];
-            load_xs<1, 1, BF16X>(d, xcol, 1, k, xv);
+            load_xs<1, 1, XM>(d, xcol, 1, k, xv);
 #pragma unroll
             for (int r = 0; r < R; ++r) sym_step_ptx(st, w, pw, acc[0][r], xv[0], tb, magic);
         }
@@ -494,7 +506,7 @@ __device__ __forceinline__ void decode_pass_windowed(uint32_t pos, const int (&x
 
 // Sets up a pass over tiles [t0, t0+kk) (consecutive), staging when possible,
 // and decodes it.  Streams j >= kk replay stream kk-1 with zero activation.
-template <int R, int K, int NACC, bool BF16X>
+template <int R, int K, int NACC, int XM>
 __device__ __forceinline__ void run_pass(const MatDev& d, const uint32_t*, uint16_t* stage,
                                          int64_t t0, int kk, const int (&xcol)[K],
                                          float (&acc)[NACC][R], int& bad, int lane) {
@@ -510,18 +522,18 @@ __device__ __forceinline__ void run_pass(const MatDev& d, const uint32_t*, uint1
         const uint32_t sbase = static_cast<uint32_t>(reinterpret_cast<uint8_t*>(stage) - g_smem);
 #pragma unroll
         for (int j = 0; j < K; ++j) pos[j] = sbase + 2u * (pos[j] - w0 + head);
-        decode_pass<R, K, NACC, BF16X, true>(pos, xcol, kk, d, acc, bad);
+        decode_pass<R, K, NACC, XM, true>(pos, xcol, kk, d, acc, bad);
         __syncwarp();   // stage is rewritten by the next pass
     } else {
         const uint64_t limit = d.nwords >= 0 ? (uint64_t)d.nwords : (d.wlimit > 0 ? (uint64_t)d.wlimit : 0);
         if constexpr (K == 1 && NACC == 1 && kStageBytes >= 32 * 32) {
             if (limit > 0) {
-                decode_pass_windowed<R, BF16X>(pos[0], xcol, d, acc, bad, stage, lane, limit);
+                decode_pass_windowed<R, XM>(pos[0], xcol, d, acc, bad, stage, lane, limit);
                 __syncwarp();   // stage is rewritten by the next pass
                 return;
             }
         }
-        decode_pass<R, K, NACC, BF16X, false>(pos, xcol, kk, d, acc, bad);
+        decode_pass<R, K, NACC, XM, false>(pos, xcol, kk, d, acc, bad);
     }
 }
 
@@ -541,7 +553,7 @@ template <int R>
 __device__ __forceinline__ void colmode_epilogue(const MatDev& d, int rb, int seg, float s, int lane,
                                                  uint16_t* stage, int warp, int nactive);
 
-template <int R, int K, bool BF16X>
+template <int R, int K, int XM>
 __device__ void colmode_item(const MatDev& d, int item, const uint32_t* tab, uint16_t* stage,
                              int lane, int& bad, int warp, int nactive) {
     const int rb = item / d.nseg;
@@ -556,7 +568,7 @@ __device__ void colmode_item(const MatDev& d, int item, const uint32_t* tab, uin
         int xcol[K];
 #pragma unroll
         for (int j = 0; j < K; ++j) xcol[j] = (cb0 + (j < kk ? j : 0)) * d.C + lane;
-        run_pass<R, K, 1, BF16X>(d, tab, stage, (int64_t)rb * d.ncb + cb0, kk, xcol, acc, bad, lane);
+        run_pass<R, K, 1, XM>(d, tab, stage, (int64_t)rb * d.ncb + cb0, kk, xcol, acc, bad, lane);
     }
     colmode_epilogue<R>(d, rb, seg, reduce_scatter<R>(acc[0], lane) * kInvCodeScale, lane, stage, warp, nactive);
 }
@@ -613,14 +625,14 @@ __device__ __forceinline__ void colmode_epilogue(const MatDev& d, int rb, int se
 
 // warp / nactive: this warp's index and the CTA's number of working warps
 // (used only when d.combine is set: the step kernel, one item per warp).
-template <int R, bool BF16X>
+template <int R, int XM>
 __device__ __forceinline__ void process_item(const MatDev& d, int item, const uint32_t* tab,
                                              uint16_t* stage, int lane, int& bad, int warp, int nactive) {
     switch (d.kcol) {
-        case 1: colmode_item<R, 1, BF16X>(d, item, tab, stage, lane, bad, warp, nactive); break;
-        case 2: colmode_item<R, 2, BF16X>(d, item, tab, stage, lane, bad, warp, nactive); break;
-        case 3: colmode_item<R, 3, BF16X>(d, item, tab, stage, lane, bad, warp, nactive); break;
-        default: colmode_item<R, 4, BF16X>(d, item, tab, stage, lane, bad, warp, nactive); break;
+        case 1: colmode_item<R, 1, XM>(d, item, tab, stage, lane, bad, warp, nactive); break;
+        case 2: colmode_item<R, 2, XM>(d, item, tab, stage, lane, bad, warp, nactive); break;
+        case 3: colmode_item<R, 3, XM>(d, item, tab, stage, lane, bad, warp, nactive); break;
+        default: colmode_item<R, 4, XM>(d, item, tab, stage, lane, bad, warp, nactive); break;
     }
 }
 
@@ -641,7 +653,7 @@ __global__ void __launch_bounds__(kThreads, RB_MINB) gemv_matrix_kernel(MatDev d
     // and is the slowest, so it starts in the first wave.
     int bad = 0;
     for (int i = blockIdx.x * kWarps + warp; i < d.nitems; i += gridDim.x * kWarps)
-        process_item<R, BF16X>(d, d.nitems - 1 - i, tab, stage, lane, bad, warp, 0);
+        process_item<R, BF16X ? kXBf16 : 0>(d, d.nitems - 1 - i, tab, stage, lane, bad, warp, 0);
 }
 
 // Tiles [t_begin, t_end) of a work item (consecutive in stream order).
@@ -732,8 +744,8 @@ __global__ void __launch_bounds__(kThreads, RB_MINB) gemv_step_kernel(const Step
     if (warp >= ch.nitems) return;
     int bad = 0;
     const MatDev dl = d;
-    if (dl.step != nullptr) process_item<R, true>(dl, ch.item0 + warp, tab, stage, lane, bad, warp, ch.nitems);
-    else process_item<R, false>(dl, ch.item0 + warp, tab, stage, lane, bad, warp, ch.nitems);
+    if (dl.step != nullptr) process_item<R, kXBf16>(dl, ch.item0 + warp, tab, stage, lane, bad, warp, ch.nitems);
+    else process_item<R, 0>(dl, ch.item0 + warp, tab, stage, lane, bad, warp, ch.nitems);
 }
 
 // One symbol of a staged stream returning kCodeScale*code (no FMA): the
@@ -1342,14 +1354,15 @@ static size_t align16(size_t v) { return (v + 15) & ~size_t(15); }
 // of a row block add up in shared memory.
 static int chunk_items(const MatDev& d) { return d.combine ? (kWarps / d.nseg) * d.nseg : kWarps; }
 
-static int layout_step(const RansGemvDesc* descs, int n, int R, StepLayout& L) {
-    L.mats.clear();
-    if (count_chunks(descs, n, R, &L.mats) < 0) return -2;
+// Work decomposition of a group of matrices that run together -- one step
+// launch, or one phase of a chain -- starting from plan_matrix(d, R, 0):
+// latency-bound groups are split into segments, groups of a few waves cut
+// into row segments.  Adds the segment counters and partials the group needs;
+// returns true when the group was planned as latency-bound (split).
+static bool plan_group(std::vector<MatDev>& mats, int R, int64_t& ncounters, int64_t& npartials) {
     int64_t items = 0;
-    for (const MatDev& d : L.mats) items += d.nitems;
+    for (const MatDev& d : mats) items += d.nitems;
     const bool split = items * 2 < split_target();
-    int64_t ncounters = 0, npartials = 0;
-    L.nchunks = 0;
     if (split) {
         // Split column-mode matrices into segments of T consecutive tiles,
         // decoded as T interleaved streams in one pass.  Start from T = 1 (the
@@ -1358,15 +1371,15 @@ static int layout_step(const RansGemvDesc* descs, int n, int R, StepLayout& L) {
         // divides ncb (T <= 4): a second, mostly idle wave would cost a whole
         // serial chain, more T costs only interleaving.
         const int64_t W = split_target();
-        std::vector<int> T(L.mats.size(), 0);
+        std::vector<int> T(mats.size(), 0);
         int64_t total = 0;
-        for (size_t i = 0; i < L.mats.size(); ++i) {
-            const MatDev& d = L.mats[i];
+        for (size_t i = 0; i < mats.size(); ++i) {
+            const MatDev& d = mats[i];
             if (d.ncb > 1) T[i] = 1;
             total += T[i] ? (int64_t)d.nrb * d.ncb : d.nitems;
         }
         auto next_t = [&](size_t i) {
-            const MatDev& d = L.mats[i];
+            const MatDev& d = mats[i];
             for (int t = T[i] + 1; t <= 4 && (int64_t)t * R * d.C <= pass_symbols(d); ++t)
                 if (d.ncb % t == 0) return t;
             return 0;
@@ -1374,19 +1387,19 @@ static int layout_step(const RansGemvDesc* descs, int n, int R, StepLayout& L) {
         while (total > W) {
             size_t best = SIZE_MAX;
             int64_t best_items = 0;
-            for (size_t i = 0; i < L.mats.size(); ++i) {
+            for (size_t i = 0; i < mats.size(); ++i) {
                 if (!T[i] || !next_t(i)) continue;
-                const int64_t it = (int64_t)L.mats[i].nrb * (L.mats[i].ncb / T[i]);
+                const int64_t it = (int64_t)mats[i].nrb * (mats[i].ncb / T[i]);
                 if (it > best_items) { best_items = it; best = i; }
             }
             if (best == SIZE_MAX) break;
             const int t = next_t(best);
-            total -= best_items - (int64_t)L.mats[best].nrb * (L.mats[best].ncb / t);
+            total -= best_items - (int64_t)mats[best].nrb * (mats[best].ncb / t);
             T[best] = t;
         }
-        for (size_t i = 0; i < L.mats.size(); ++i) {
+        for (size_t i = 0; i < mats.size(); ++i) {
             if (!T[i]) continue;
-            MatDev& d = L.mats[i];
+            MatDev& d = mats[i];
             d.kcol = T[i];
             d.nseg = d.ncb / T[i];
             d.cbs = T[i];
@@ -1408,7 +1421,7 @@ static int layout_step(const RansGemvDesc* descs, int n, int R, StepLayout& L) {
         // let the makespan model of plan_matrix cut its rows into equal
         // segments of passes (same K); segments meet in `partials`, as above.
         const int64_t W = split_target();
-        for (MatDev& d : L.mats) {
+        for (MatDev& d : mats) {
             if (d.ncb <= d.kcol) continue;
             const int share = (int)std::max<int64_t>(1, W * d.nitems / items);
             MatDev sp = d;
@@ -1425,6 +1438,15 @@ static int layout_step(const RansGemvDesc* descs, int n, int R, StepLayout& L) {
             }
         }
     }
+    return split;
+}
+
+static int layout_step(const RansGemvDesc* descs, int n, int R, StepLayout& L) {
+    L.mats.clear();
+    if (count_chunks(descs, n, R, &L.mats) < 0) return -2;
+    int64_t ncounters = 0, npartials = 0;
+    const bool split = plan_group(L.mats, R, ncounters, npartials);
+    L.nchunks = 0;
     for (MatDev& d : L.mats) L.nchunks += (d.nitems + chunk_items(d) - 1) / chunk_items(d);
     // Launches of two or more waves of items read activations through a
     // prescaled fp32 copy (5% faster on a whole decoder step); shorter ones
@@ -1557,7 +1579,7 @@ static int plan_step(const RansGemvDesc* descs, const void* const* peer_y, int n
             ch[c].desc = i;
             ch[c].item0 = it;
             ch[c].nitems = mats[i].nitems - it < cs ? mats[i].nitems - it : cs;
-            ch[c].pad_ = 0;
+            ch[c].phase = 0;
             ++c;
         }
     }
@@ -1669,6 +1691,396 @@ extern "C" int rans_gemv_step_launch(int R, const void* workspace, int grid, cud
     }
 }
 
+namespace rb200 {
+
+// ------------------------------------------------------------ chain launcher
+// Every projection of a decoder step, in dependency order, from ONE persistent
+// grid.  A decoder step is a chain of phases -- per layer {q,k,v} -> o ->
+// {gate,up} -> down -- and phase p+1 reads what phase p wrote.  The chain
+// kernel runs as many CTAs as fit on the GPU at once; each takes chunks (up to
+// 8 items of one matrix) from a queue ordered by phase with one atomic, loads
+// its matrix's table, warms L2 with the chunk's words, and, for a chunk of
+// phase p > 0, waits until every chunk of phase p-1 is complete (and, when the
+// projections are row-sharded over several GPUs, until every rank has
+// signalled phase p-1).  Every chunk of phase p-1 was handed to a CTA that is
+// already running before any chunk of phase p was, so the waits always end
+// without any co-residency assumption.  Each wait is bounded: after the
+// plan's timeout the kernel records the phase, every CTA leaves, and
+// rans_gemv_chain_status reports it (the context stays usable).
+//
+// Memory ordering.  A CTA finishing a chunk: bar.sync, then one thread fences
+// (gpu scope; system scope when its rows were also stored to peer GPUs) and
+// increments the phase's completion counter.  The CTA that completes a phase
+// on a multi-GPU plan then adds 1 to that phase's arrival counter on every
+// rank (red.release.sys).  A waiting thread reads the counters with
+// ld.acquire, then bar.sync; activations are read through L2 (ld.global.cg).
+//
+// The last CTA to leave resets the queue and completion counters and counts
+// the launch (epoch); arrival counters only grow, and a multi-GPU wait of
+// launch e needs nranks * (e + 1) arrivals.  A wait that ran out leaves the
+// status set: launches return at once until rans_gemv_chain_status has read
+// and cleared it (multi-GPU plans must then be planned again on every rank).
+constexpr int32_t kChainTimeout = 1;
+
+struct ChainHeader {
+    int ndesc, nchunks, R, nphases;
+    int npeer, rank, pad0, pad1;
+    int64_t phase_off;         // int32 phase_end[nphases]: chunks [phase_end[p-1], phase_end[p]) are phase p
+    int64_t ctl_off;           // ChainCtl, then uint32 done[nphases]
+    int64_t timeout_ns;        // bound of every dependency wait
+    uint32_t* arrive;          // this rank's arrival counters [nphases] (multi-GPU), or null
+    uint32_t* arrive_peer[kMaxPeers];   // every rank's arrival counters, as addresses valid on this GPU
+};
+
+struct ChainCtl {
+    uint32_t queue;            // next chunk to hand out
+    uint32_t exited;           // CTAs that have left this launch
+    uint32_t epoch;            // launches completed on this workspace
+    int32_t status;            // 0, or kChainTimeout once a wait ran out (sticky until read)
+    int32_t where;             // phase whose wait ran out
+    uint32_t pad[3];
+};
+
+__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void red_release_sys(uint32_t* p, uint32_t v) {
+    asm volatile("red.release.sys.global.add.u32 [%0], %1;\n" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;\n" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ uint32_t phase_chunks(const int* phase_end, int p) {
+    return (uint32_t)(phase_end[p] - (p > 0 ? phase_end[p - 1] : 0));
+}
+
+// Control block and completion counters of a chain workspace.
+__device__ __forceinline__ ChainCtl* chain_ctl(const ChainHeader* h) {
+    return reinterpret_cast<ChainCtl*>(const_cast<uint8_t*>(reinterpret_cast<const uint8_t*>(h)) + h->ctl_off);
+}
+__device__ __forceinline__ const int* chain_phase_end(const ChainHeader* h) {
+    return reinterpret_cast<const int*>(reinterpret_cast<const uint8_t*>(h) + h->phase_off);
+}
+__device__ __forceinline__ const Chunk* chain_chunks(const ChainHeader* h) {
+    return reinterpret_cast<const Chunk*>(reinterpret_cast<const MatDev*>(h + 1) + h->ndesc);
+}
+
+// Thread 0 of a CTA: wait until phase p is complete -- all its chunks on this
+// GPU and, multi-GPU, every rank's arrival for this launch.  Polls with a
+// growing sleep; returns false when the wait ran out (recording it) or another
+// CTA already reported an error.
+__device__ bool chain_wait(const ChainHeader* h, int p) {
+    ChainCtl* ctl = chain_ctl(h);
+    const uint32_t* done = reinterpret_cast<const uint32_t*>(ctl + 1);
+    const uint32_t need = phase_chunks(chain_phase_end(h), p);
+    // the epoch changes only after every CTA of this launch has left
+    const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(&ctl->epoch);
+    const uint32_t need_arrive = (uint32_t)h->npeer * (epoch + 1u);
+    uint64_t t0 = 0;
+    unsigned sleep_ns = 32;
+    for (;;) {
+        const bool local = ld_acquire_gpu(done + p) >= need;
+        const bool peers = h->npeer == 0 || (int32_t)(ld_acquire_sys(h->arrive + p) - need_arrive) >= 0;
+        if (local && peers) return true;
+        if (*reinterpret_cast<volatile int32_t*>(&ctl->status) != 0) return false;
+        const uint64_t t = global_ns();
+        if (t0 == 0) {
+            t0 = t;
+        } else if (t - t0 > (uint64_t)h->timeout_ns) {
+            if (atomicCAS(&ctl->status, 0, kChainTimeout) == 0) atomicExch(&ctl->where, p);
+            return false;
+        }
+        __nanosleep(sleep_ns);
+        if (sleep_ns < 1024) sleep_ns *= 2;
+    }
+}
+
+template <int R>
+__global__ void __launch_bounds__(kThreads, RB_MINB) gemv_chain_kernel(const ChainHeader* __restrict__ hdr) {
+    __shared__ int s_chunk, s_go;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const SmemMap sm = smem_map(warp);
+    int cur = -1;   // matrix whose table is in shared memory
+    for (;;) {
+        if (threadIdx.x == 0) {
+            ChainCtl* ctl = chain_ctl(hdr);
+            int c = hdr->nchunks;
+            if (*reinterpret_cast<volatile int32_t*>(&ctl->status) == 0) c = (int)atomicAdd(&ctl->queue, 1u);
+            s_chunk = c;
+        }
+        __syncthreads();
+        const int c = s_chunk;
+        if (c >= hdr->nchunks) break;
+        const Chunk ch = chain_chunks(hdr)[c];
+        const MatDev& d = reinterpret_cast<const MatDev*>(hdr + 1)[ch.desc];
+        // weights are immutable: the table load and the L2 warm-up of the
+        // chunk's words overlap the wait for the previous phase
+        if (ch.desc != cur) {
+            load_table(sm.tab, d.table);
+            cur = ch.desc;
+        }
+        if (threadIdx.x == 0) {
+            int go = 1;
+            if (ch.phase > 0) {
+                int64_t t0, t1, u0, u1;
+                item_tiles(d, ch.item0, t0, t1);
+                item_tiles(d, ch.item0 + ch.nitems - 1, u0, u1);
+                const uint32_t w0 = d.offs[t0 * 32];
+                const uint64_t w1 = span_end(d, u1 * 32);
+                if (w1 != UINT64_MAX && w1 > w0) prefetch_l2(d.words + w0, 2ull * (w1 - w0));
+                go = chain_wait(hdr, ch.phase - 1) ? 1 : 0;
+            }
+            s_go = go;
+        }
+        __syncthreads();
+        if (!s_go) break;
+        if (warp < ch.nitems) {
+            int bad = 0;
+            const MatDev dl = d;
+            if (dl.step != nullptr)
+                process_item<R, kXBf16 | kXCoherent>(dl, ch.item0 + warp, sm.tab, sm.stage, lane, bad, warp, ch.nitems);
+            else
+                process_item<R, kXCoherent>(dl, ch.item0 + warp, sm.tab, sm.stage, lane, bad, warp, ch.nitems);
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            const int p = chain_chunks(hdr)[s_chunk].phase;
+            if (hdr->npeer > 0) __threadfence_system();
+            else __threadfence();
+            uint32_t* done = reinterpret_cast<uint32_t*>(chain_ctl(hdr) + 1);
+            const uint32_t prev = atomicAdd(done + p, 1u);
+            if (hdr->npeer > 0 && prev + 1 == phase_chunks(chain_phase_end(hdr), p)) {
+                // this GPU's rows of the phase are everywhere: tell every rank
+                for (int q = 0; q < hdr->npeer; ++q) red_release_sys(hdr->arrive_peer[q] + p, 1u);
+            }
+        }
+    }
+    // the last CTA out resets the queue and the completion counters
+    if (threadIdx.x == 0) {
+        ChainCtl* ctl = chain_ctl(hdr);
+        __threadfence();
+        const uint32_t n = atomicAdd(&ctl->exited, 1u);
+        if (n + 1 == gridDim.x) {
+            uint32_t* done = reinterpret_cast<uint32_t*>(ctl + 1);
+            for (int p = 0; p < hdr->nphases; ++p) done[p] = 0u;
+            ctl->queue = 0u;
+            ctl->exited = 0u;
+            ctl->epoch = *reinterpret_cast<volatile uint32_t*>(&ctl->epoch) + 1u;
+            __threadfence();
+        }
+    }
+}
+
+struct ChainLayout {
+    std::vector<MatDev> mats;
+    std::vector<int> phase_end;    // per phase: one past its last chunk
+    int nphases = 0;
+    int64_t nchunks = 0;
+    size_t phase_off = 0, ctl_off = 0, counters_off = 0, partials_off = 0, bytes = 0;
+};
+
+static int layout_chain(const RansGemvDesc* descs, const int* phase, int n, int R, ChainLayout& L) {
+    if (n <= 0 || descs == nullptr || phase == nullptr) return -2;
+    int P = 0;
+    for (int i = 0; i < n; ++i) {
+        if (phase[i] < 0 || phase[i] >= n) return -2;
+        P = std::max(P, phase[i] + 1);
+    }
+    std::vector<std::vector<int>> members(P);
+    for (int i = 0; i < n; ++i) members[phase[i]].push_back(i);
+    for (int p = 0; p < P; ++p)
+        if (members[p].empty()) return -2;   // phases are numbered 0..P-1 without gaps
+    L.mats.clear();
+    if (count_chunks(descs, n, R, &L.mats) < 0) return -2;
+    int64_t ncounters = 0, npartials = 0;
+    L.phase_end.assign(P, 0);
+    L.nphases = P;
+    L.nchunks = 0;
+    for (int p = 0; p < P; ++p) {
+        // each phase runs on the whole GPU by itself: plan it like one launch
+        std::vector<MatDev> g;
+        for (int i : members[p]) g.push_back(L.mats[i]);
+        plan_group(g, R, ncounters, npartials);
+        for (size_t k = 0; k < g.size(); ++k) {
+            L.mats[members[p][k]] = g[k];
+            L.nchunks += (g[k].nitems + chunk_items(g[k]) - 1) / chunk_items(g[k]);
+        }
+        L.phase_end[p] = (int)L.nchunks;
+    }
+    L.phase_off = align16(sizeof(ChainHeader) + sizeof(MatDev) * (size_t)n + sizeof(Chunk) * (size_t)L.nchunks);
+    L.ctl_off = align16(L.phase_off + sizeof(int) * (size_t)P);
+    L.counters_off = align16(L.ctl_off + sizeof(ChainCtl) + sizeof(uint32_t) * (size_t)P);
+    L.partials_off = align16(L.counters_off + sizeof(uint32_t) * (size_t)ncounters);
+    L.bytes = align16(L.partials_off + sizeof(float) * (size_t)npartials);
+    return 0;
+}
+
+extern "C" int64_t rans_gemv_chain_workspace_bytes(const RansGemvDesc* descs, const int* phase, int n, int R) {
+    if (!valid_R(R)) return -1;
+    ChainLayout L;
+    if (layout_chain(descs, phase, n, R, L) != 0) return -2;
+    return (int64_t)L.bytes;
+}
+
+template <int R>
+static int chain_grid_t(int64_t nchunks) {
+    static unsigned long long done = 0;
+    static int resident[64] = {};
+    if (!set_smem_attr((const void*)gemv_chain_kernel<R>, &done)) return -1;
+    return (int)std::min<int64_t>(nchunks, resident_blocks((const void*)gemv_chain_kernel<R>, resident));
+}
+
+static int chain_grid(int R, int64_t nchunks) {
+    switch (R) {
+        case 1: return chain_grid_t<1>(nchunks);
+        case 2: return chain_grid_t<2>(nchunks);
+        case 4: return chain_grid_t<4>(nchunks);
+        case 8: return chain_grid_t<8>(nchunks);
+        case 16: return chain_grid_t<16>(nchunks);
+        default: return -1;
+    }
+}
+
+extern "C" int rans_gemv_chain_plan(const RansGemvDesc* descs, const int* phase, int n, int R,
+                                    const RansChainSync* sync, int timeout_ms, void* workspace,
+                                    size_t workspace_bytes, int* grid_out, cudaStream_t stream) {
+    if (!valid_R(R)) return -1;
+    if (timeout_ms <= 0) return -2;
+    if (sync != nullptr && (sync->nranks < 1 || sync->nranks > kMaxPeers || sync->rank < 0 ||
+                            sync->rank >= sync->nranks || sync->arrive == nullptr ||
+                            sync->arrive_peer == nullptr || sync->peer_y == nullptr))
+        return -2;
+    ChainLayout L;
+    if (layout_chain(descs, phase, n, R, L) != 0) return -2;
+    if (L.bytes > workspace_bytes) return -3;
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    int64_t coff = 0, poff = 0;
+    for (int i = 0; i < n; ++i) {
+        MatDev& d = L.mats[i];
+        if (d.nseg > 1 && !d.accumulate && !d.combine) {
+            d.counters = reinterpret_cast<uint32_t*>(ws + L.counters_off) + coff;
+            d.partials = reinterpret_cast<float*>(ws + L.partials_off) + poff;
+            coff += d.nrb;
+            poff += (int64_t)d.nrb * d.nseg * R;
+        }
+        if (sync != nullptr) {
+            if (d.accumulate) return -2;   // atomically accumulated rows cannot be exchanged by stores
+            d.npeer = sync->nranks;
+            for (int p = 0; p < sync->nranks; ++p)
+                d.ypeer[p] = static_cast<float*>(const_cast<void*>(sync->peer_y[(size_t)i * sync->nranks + p]));
+        }
+    }
+    // host image up to the partials (header, descriptors, chunks, phase ends,
+    // zeroed control block and segment counters)
+    std::vector<uint8_t> host(L.partials_off, 0);
+    ChainHeader* h = reinterpret_cast<ChainHeader*>(host.data());
+    h->ndesc = n;
+    h->nchunks = (int)L.nchunks;
+    h->R = R;
+    h->nphases = L.nphases;
+    h->npeer = sync ? sync->nranks : 0;
+    h->rank = sync ? sync->rank : 0;
+    h->phase_off = (int64_t)L.phase_off;
+    h->ctl_off = (int64_t)L.ctl_off;
+    h->timeout_ns = (int64_t)timeout_ms * 1000000ll;
+    if (sync) {
+        h->arrive = static_cast<uint32_t*>(sync->arrive);
+        for (int p = 0; p < sync->nranks; ++p) h->arrive_peer[p] = static_cast<uint32_t*>(sync->arrive_peer[p]);
+    }
+    MatDev* md = reinterpret_cast<MatDev*>(h + 1);
+    Chunk* ch = reinterpret_cast<Chunk*>(md + n);
+    for (int i = 0; i < n; ++i) md[i] = L.mats[i];
+    int64_t c = 0;
+    auto item_cost = [&](const MatDev& d) -> int64_t { return (int64_t)R * d.cbs * d.C; };
+    for (int p = 0; p < L.nphases; ++p) {
+        const int64_t c0 = c;
+        for (int i = 0; i < n; ++i) {
+            if (phase[i] != p) continue;
+            const int cs = chunk_items(md[i]);
+            for (int it = 0; it < md[i].nitems; it += cs) {
+                ch[c].desc = i;
+                ch[c].item0 = it;
+                ch[c].nitems = md[i].nitems - it < cs ? md[i].nitems - it : cs;
+                ch[c].phase = p;
+                ++c;
+            }
+        }
+        // longest chunks of the phase first: its last CTAs to start run the shortest
+        std::stable_sort(ch + c0, ch + c, [&](const Chunk& a, const Chunk& b) {
+            return item_cost(md[a.desc]) > item_cost(md[b.desc]);
+        });
+    }
+    int* pe = reinterpret_cast<int*>(host.data() + L.phase_off);
+    for (int p = 0; p < L.nphases; ++p) pe[p] = L.phase_end[p];
+    const int grid = chain_grid(R, L.nchunks);
+    if (grid <= 0) return (int)cudaErrorInvalidConfiguration;
+    cudaError_t e = cudaMemcpyAsync(workspace, host.data(), host.size(), cudaMemcpyHostToDevice, stream);
+    if (e != cudaSuccess) return (int)e;
+    if (sync != nullptr) {
+        // this rank's arrival counters start at zero; the caller makes every
+        // rank finish planning (a host barrier) before any rank launches
+        e = cudaMemsetAsync(sync->arrive, 0, sizeof(uint32_t) * (size_t)L.nphases, stream);
+        if (e != cudaSuccess) return (int)e;
+    }
+    // the pageable source must stay valid until the copy has been staged
+    e = cudaStreamSynchronize(stream);
+    if (e != cudaSuccess) return (int)e;
+    if (grid_out) *grid_out = grid;
+    return 0;
+}
+
+template <int R>
+static int launch_chain_t(const void* ws, int grid, cudaStream_t stream) {
+    static unsigned long long done = 0;
+    set_smem_attr((const void*)gemv_chain_kernel<R>, &done);
+    gemv_chain_kernel<R><<<grid, kThreads, kSmemBytes, stream>>>(static_cast<const ChainHeader*>(ws));
+    return (int)cudaGetLastError();
+}
+
+extern "C" int rans_gemv_chain_launch(int R, const void* workspace, int grid, cudaStream_t stream) {
+    if (grid <= 0) return 0;
+    switch (R) {
+        case 1: return launch_chain_t<1>(workspace, grid, stream);
+        case 2: return launch_chain_t<2>(workspace, grid, stream);
+        case 4: return launch_chain_t<4>(workspace, grid, stream);
+        case 8: return launch_chain_t<8>(workspace, grid, stream);
+        case 16: return launch_chain_t<16>(workspace, grid, stream);
+        default: return -1;
+    }
+}
+
+extern "C" int rans_gemv_chain_status(void* workspace, int* phase_out, cudaStream_t stream) {
+    if (workspace == nullptr) return -2;
+    ChainHeader h;
+    ChainCtl ctl;
+    cudaError_t e = cudaMemcpyAsync(&h, workspace, sizeof(h), cudaMemcpyDeviceToHost, stream);
+    if (e != cudaSuccess) return (int)e;
+    if ((e = cudaStreamSynchronize(stream)) != cudaSuccess) return (int)e;
+    uint8_t* ctl_dev = static_cast<uint8_t*>(workspace) + h.ctl_off;
+    e = cudaMemcpyAsync(&ctl, ctl_dev, sizeof(ctl), cudaMemcpyDeviceToHost, stream);
+    if (e != cudaSuccess) return (int)e;
+    if ((e = cudaStreamSynchronize(stream)) != cudaSuccess) return (int)e;
+    if (phase_out) *phase_out = ctl.status != 0 ? ctl.where : -1;
+    if (ctl.status == 0) return 0;
+    // read and cleared: the next launch runs again
+    e = cudaMemsetAsync(ctl_dev + offsetof(ChainCtl, status), 0, 2 * sizeof(int32_t), stream);
+    if (e != cudaSuccess) return (int)e;
+    if ((e = cudaStreamSynchronize(stream)) != cudaSuccess) return (int)e;
+    return -5;
+}
+
+}  // namespace rb200
+
 // ------------------------------------------------- step launcher, no allocation
 // Some callers cannot allocate device memory at the point where they run a
 // decoder step: a framework whose caching allocator owns the whole pool (a
@@ -1759,7 +2171,7 @@ extern "C" int rans_gemv_step_noalloc(const RansGemvDesc* descs, int n, int R, c
             ch[c].desc = i;
             ch[c].item0 = it;
             ch[c].nitems = md[i].nitems - it < kWarps ? md[i].nitems - it : kWarps;
-            ch[c].pad_ = 0;
+            ch[c].phase = 0;
             ++c;
         }
     }

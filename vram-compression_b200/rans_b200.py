@@ -10,8 +10,9 @@ the same way:
   RansMatrix(enc, step, lib)  kernel/rans.py:127-162 device-resident matrix
   Int4Matrix(codes, step, lib) kernel/rans.py:165-185 fixed-rate baseline
 
-plus the B200 additions: RansMatrix.gemv_bf16 (step folded into the kernel)
-and RansStep (every projection of a decoder step from one grid).
+plus the B200 additions: RansMatrix.gemv_bf16 (step folded into the kernel),
+RansStep (every projection of a decoder step from one grid) and RansChain (a
+decoder step as a chain of dependent phases from one persistent grid).
 
 There is no CPU fallback: every GEMV/decode goes through librans_b200.so and
 raises if the library or a CUDA device is missing.
@@ -30,7 +31,7 @@ M = 1 << SCALE_BITS
 RANS_L = 1 << 16
 OFFSET = 128
 PAD_WORDS = 8
-ABI_VERSION = 2
+ABI_VERSION = 3
 
 _vp, _i32, _i64, _sz = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_size_t
 
@@ -40,6 +41,15 @@ class RansGemvDesc(ctypes.Structure):
     _fields_ = [("words", _vp), ("offs", _vp), ("table", _vp), ("x", _vp), ("step", _vp),
                 ("y", _vp), ("nwords", _i64), ("rows", ctypes.c_int32), ("cols", ctypes.c_int32),
                 ("C", ctypes.c_int32), ("reserved", ctypes.c_int32)]
+
+
+class RansChainSync(ctypes.Structure):
+    """ctypes mirror of the C struct RansChainSync (include/rans_b200.h)."""
+    _fields_ = [("nranks", ctypes.c_int32), ("rank", ctypes.c_int32), ("arrive", _vp),
+                ("arrive_peer", _vp), ("peer_y", _vp)]
+
+
+CHAIN_TIMEOUT = -5      # rans_gemv_chain_status: a dependency wait ran out
 
 
 def _bind(lib):
@@ -72,6 +82,14 @@ def _bind(lib):
     lib.rans_escape_gemv.restype = _i32
     lib.rans_escape_decode.argtypes = [_vp, _vp, _vp, _i32, _vp, _vp, _i32, _vp]
     lib.rans_escape_decode.restype = _i32
+    lib.rans_gemv_chain_workspace_bytes.argtypes = [_vp, _vp, _i32, _i32]
+    lib.rans_gemv_chain_workspace_bytes.restype = _i64
+    lib.rans_gemv_chain_plan.argtypes = [_vp, _vp, _i32, _i32, _vp, _i32, _vp, _sz, _vp, _vp]
+    lib.rans_gemv_chain_plan.restype = _i32
+    lib.rans_gemv_chain_launch.argtypes = [_i32, _vp, _i32, _vp]
+    lib.rans_gemv_chain_launch.restype = _i32
+    lib.rans_gemv_chain_status.argtypes = [_vp, _vp, _vp]
+    lib.rans_gemv_chain_status.restype = _i32
     lib.rans_b200_abi_version.argtypes = []
     lib.rans_b200_abi_version.restype = _i32
     return lib
@@ -142,6 +160,21 @@ def build_table(sym, nthreads: int = 0):
     return freq.astype(np.int64), cum.astype(np.int64), table
 
 
+def table_of_codes(codes, nthreads: int = 0) -> np.ndarray:
+    """The 12-bit slot table (uint32[4096]) of integer codes in [-128, 127]
+    (kernel/rans.py:34-51), e.g. of a whole matrix whose row ranges are
+    encoded separately with encode(..., table=)."""
+    lib = _lib()
+    c8 = codes_to_int8(codes).ravel()
+    table = np.zeros(M, np.uint32)
+    freq = np.zeros(256, np.int32)
+    cum = np.zeros(256, np.int32)
+    if lib.rans_build_table_host(c8.ctypes.data, c8.size, table.ctypes.data, freq.ctypes.data,
+                                 cum.ctypes.data, nthreads) != 0:
+        raise AssertionError("degenerate distribution (single symbol)")
+    return table
+
+
 # ------------------------------------------------------------------ encoding
 def lane_order(sym, R: int, C: int) -> np.ndarray:
     rows, cols = sym.shape
@@ -151,9 +184,14 @@ def lane_order(sym, R: int, C: int) -> np.ndarray:
     return a.transpose(0, 2, 4, 3, 1).reshape(-1, (C // 32) * R)
 
 
-def encode(codes, R: int, C: int, nthreads: int = 0) -> dict:
+def encode(codes, R: int, C: int, nthreads: int = 0, table=None) -> dict:
     """Encode integer codes in [-128, 127]; returns the reference's dict
-    (words uint16, offs uint32, table uint32, R, C, shape, bit accounting)."""
+    (words uint16, offs uint32, table uint32, R, C, shape, bit accounting).
+
+    table: optional slot table to encode with instead of the one built from
+    `codes` -- e.g. the table of a whole matrix when encoding a row-block
+    range of it (the streams are then exactly those of the whole matrix's
+    encoding; every code must have a non-zero frequency in the table)."""
     lib = _lib()
     codes = np.asarray(codes)
     if codes.ndim != 2:
@@ -162,12 +200,21 @@ def encode(codes, R: int, C: int, nthreads: int = 0) -> dict:
     if not (rows % R == 0 and cols % C == 0 and C % 32 == 0):
         raise AssertionError("rows % R, cols % C and C % 32 must be 0")
     c8 = codes_to_int8(codes)
-    table = np.zeros(M, np.uint32)
-    freq = np.zeros(256, np.int32)
-    cum = np.zeros(256, np.int32)
-    if lib.rans_build_table_host(c8.ctypes.data, c8.size, table.ctypes.data, freq.ctypes.data,
-                                 cum.ctypes.data, nthreads) != 0:
-        raise AssertionError("degenerate distribution (single symbol)")
+    if table is None:
+        table = np.zeros(M, np.uint32)
+        freq = np.zeros(256, np.int32)
+        cum = np.zeros(256, np.int32)
+        if lib.rans_build_table_host(c8.ctypes.data, c8.size, table.ctypes.data, freq.ctypes.data,
+                                     cum.ctypes.data, nthreads) != 0:
+            raise AssertionError("degenerate distribution (single symbol)")
+    else:
+        table = np.ascontiguousarray(table, np.uint32)
+        if table.shape != (M,):
+            raise ValueError("table must hold 4096 slots")
+        freq = np.bincount((table & 0xFF).astype(np.int64), minlength=256).astype(np.int32)
+        present = np.bincount(c8.ravel().astype(np.int16) + OFFSET, minlength=256) > 0
+        if np.any(freq[present] == 0):
+            raise ValueError("a code has no slot in the given table")
     cap = lib.rans_encode_bound(rows, cols, R, C)
     nstreams = rows * cols * 32 // (R * C)
     words = np.empty(cap, np.uint16)
@@ -380,3 +427,83 @@ class RansStep:
         rc = self.lib.rans_gemv_step_launch(self.R, self.workspace.data_ptr(), self.grid, _stream(torch))
         _check(rc, "rans_gemv_step_launch")
         return self.ys
+
+
+class ChainTimeout(RuntimeError):
+    """A dependency wait of the chain kernel ran out (the phase it waited for
+    never completed in time); that launch's outputs are incomplete."""
+
+    def __init__(self, phase):
+        super().__init__(f"chain launch: the wait for phase {phase} ran out")
+        self.phase = phase
+
+
+class RansChain:
+    """A decoder step as a chain of dependent phases, from ONE persistent grid.
+
+    mats/xs/ys as for RansStep; phases[i] is matrix i's phase (0..P-1): every
+    matrix of phase p+1 starts only when all of phase p is done, so phase
+    p+1's x may be phase p's y (mark such matrices in prescaled_x, a bool or
+    one flag per matrix: fp32 activations already multiplied by the step;
+    the others take bf16 x with the step applied in-kernel).  One call is one
+    kernel launch.
+    sync: optional (nranks, rank, arrive_ptr, arrive_peer_ptrs, peers) of a
+    row-sharded chain over several GPUs (see rans_dist.ShardedChain).
+    timeout_ms bounds every wait inside the kernel; check() reports a wait
+    that ran out (ChainTimeout).
+    """
+
+    def __init__(self, mats, xs, ys, phases, lib=None, prescaled_x=False, timeout_ms=2000, sync=None):
+        torch = _torch()
+        self.lib = _lib(lib)
+        if not mats or len(phases) != len(mats) or len(xs) != len(mats) or len(ys) != len(mats):
+            raise ValueError("one activation, output and phase per matrix")
+        R = mats[0].R
+        if any(m.R != R for m in mats):
+            raise ValueError("all matrices of a chain must share R")
+        self.R = R
+        self.mats, self.xs, self.ys = list(mats), list(xs), list(ys)
+        self.phases = [int(p) for p in phases]
+        pre = list(prescaled_x) if isinstance(prescaled_x, (list, tuple)) else [bool(prescaled_x)] * len(mats)
+        if len(pre) != len(mats):
+            raise ValueError("prescaled_x: one flag per matrix")
+        arr = (RansGemvDesc * len(mats))(*[m.desc(x, y, step=not p) for m, x, y, p in zip(mats, xs, ys, pre)])
+        ph = (ctypes.c_int * len(mats))(*self.phases)
+        self._descs, self._ph = arr, ph
+        nbytes = self.lib.rans_gemv_chain_workspace_bytes(ctypes.addressof(arr), ctypes.addressof(ph), len(mats), R)
+        if nbytes < 0:
+            raise ValueError(f"bad chain description ({nbytes})")
+        self.workspace = torch.empty(int(nbytes), dtype=torch.uint8, device=mats[0].device)
+        sync_p = None
+        if sync is not None:
+            nranks, rank, arrive, arrive_peer, peers = sync
+            if len(arrive_peer) != nranks or len(peers) != len(mats) or any(len(p) != nranks for p in peers):
+                raise ValueError("one arrival address per rank and one peer address per rank and matrix")
+            self._arrive_peer = (ctypes.c_void_p * nranks)(*[int(a) for a in arrive_peer])
+            self._peer_y = (ctypes.c_void_p * (len(mats) * nranks))(*[int(a) for p in peers for a in p])
+            self._sync = RansChainSync(nranks, rank, int(arrive), ctypes.addressof(self._arrive_peer),
+                                       ctypes.addressof(self._peer_y))
+            sync_p = ctypes.addressof(self._sync)
+        grid = ctypes.c_int(0)
+        rc = self.lib.rans_gemv_chain_plan(ctypes.addressof(arr), ctypes.addressof(ph), len(mats), R, sync_p,
+                                           int(timeout_ms), self.workspace.data_ptr(), int(nbytes),
+                                           ctypes.byref(grid), _stream(torch))
+        _check(rc, "rans_gemv_chain_plan")
+        self.grid = grid.value
+        self.kernels = 1
+
+    def __call__(self):
+        torch = _torch()
+        rc = self.lib.rans_gemv_chain_launch(self.R, self.workspace.data_ptr(), self.grid, _stream(torch))
+        _check(rc, "rans_gemv_chain_launch")
+        return self.ys
+
+    def check(self):
+        """Synchronise and raise ChainTimeout if a wait of the launches so far
+        ran out (reading it clears it)."""
+        torch = _torch()
+        phase = ctypes.c_int(-1)
+        rc = self.lib.rans_gemv_chain_status(self.workspace.data_ptr(), ctypes.byref(phase), _stream(torch))
+        if rc == CHAIN_TIMEOUT:
+            raise ChainTimeout(phase.value)
+        _check(rc, "rans_gemv_chain_status")

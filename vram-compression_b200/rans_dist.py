@@ -12,6 +12,11 @@ in one step launch, and the outputs are exchanged in one of two ways:
   nccl   the step writes local rows, then one all-gather per call
          (`gather_rows`, any backend: NCCL on GPUs, gloo on CPU).
 
+ShardedChain runs a dependency-ordered decoder step (rans_b200.RansChain)
+the same way: one launch per rank, each phase's rows stored into every rank's
+full outputs, and an in-kernel wait per phase for every rank's arrival signal
+(bounded: a wait that runs out is reported by check()).
+
 The reference has no multi-GPU path; this is the exchange step its survey
 describes (one all-gather of y per projection), fused into the kernel.
 """
@@ -178,3 +183,76 @@ class ShardedStep:
         group is destroyed."""
         self.step = None
         self.hdl = None
+
+
+def _symm_rendezvous(t):
+    import torch.distributed as dist
+    import torch.distributed._symmetric_memory as symm_mem
+    try:
+        return symm_mem.rendezvous(t, dist.group.WORLD)
+    except Exception:
+        symm_mem.enable_symm_mem_for_group(dist.group.WORLD.group_name)
+        return symm_mem.rendezvous(t, dist.group.WORLD)
+
+
+class ShardedChain:
+    """This rank's share of a dependency-ordered decoder step (phases) whose
+    projections are row-sharded over the ranks of the default process group.
+
+    mats / full_rows / xs as for ShardedStep; phases[i] is projection i's
+    phase.  One call is one kernel launch on this rank: phase p+1 starts once
+    every rank has stored its rows of phase p into every rank's `y_full`
+    (symmetric memory) and signalled it.  After a call, `full[i]` is
+    projection i's complete output on this rank.  Every rank must call the
+    same number of times; check() synchronises and raises
+    rans_b200.ChainTimeout if a wait ran out (then build the chain again on
+    every rank).
+    """
+
+    def __init__(self, mats, full_rows, xs, phases, timeout_ms: int = 5000, lib=None, prescaled_x=False):
+        import torch
+        import torch.distributed as dist
+        import torch.distributed._symmetric_memory as symm_mem
+        if len(mats) != len(full_rows) or len(xs) != len(mats) or len(phases) != len(mats):
+            raise ValueError("one shard, one full row count, one activation and one phase per projection")
+        self.rank, self.world = dist.get_rank(), dist.get_world_size()
+        R = mats[0].R
+        self.layout = ShardLayout(full_rows, R, self.world)
+        for i, m in enumerate(mats):
+            if m.rows != self.layout.nrows[i][self.rank]:
+                raise ValueError(f"projection {i}: shard has {m.rows} rows, "
+                                 f"rank {self.rank} owns {self.layout.nrows[i][self.rank]}")
+        dev = mats[0].device
+        nphases = max(int(p) for p in phases) + 1
+        self.y_full = symm_mem.empty(self.layout.total, dtype=torch.float32, device=dev)
+        self.y_full.zero_()
+        self.hdl = _symm_rendezvous(self.y_full)
+        self.arrive = symm_mem.empty(max(nphases, 4), dtype=torch.int32, device=dev)
+        self.arrive.zero_()
+        self.hdl_arrive = _symm_rendezvous(self.arrive)
+        peers = self.layout.peer_addresses([int(p) for p in self.hdl.buffer_ptrs], self.rank)
+        arrive_peer = [int(p) for p in self.hdl_arrive.buffer_ptrs]
+        sl = self.layout.local_slices(self.rank)
+        ys = [self.y_full[a:b] for a, b in sl]
+        torch.cuda.synchronize()
+        self.chain = rb.RansChain(mats, xs, ys, phases, lib=lib, prescaled_x=prescaled_x, timeout_ms=timeout_ms,
+                                  sync=(self.world, self.rank, self.arrive.data_ptr(), arrive_peer, peers))
+        # every rank has zeroed its arrival counters before any rank launches
+        dist.barrier()
+        self.full = [self.y_full[int(self.layout.F[i]):int(self.layout.F[i]) + self.layout.rows[i]]
+                     for i in range(len(mats))]
+        self.kernels = 1
+
+    def __call__(self):
+        self.chain()
+        return self.full
+
+    def check(self):
+        self.chain.check()
+
+    def close(self):
+        """Drop the plan and the symmetric-memory handles before the process
+        group is destroyed."""
+        self.chain = None
+        self.hdl = None
+        self.hdl_arrive = None
