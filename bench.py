@@ -573,20 +573,22 @@ def main():
         graph_ms = a.elapsed_time(b) / args.steps
         chain()
         torch.cuda.synchronize()
-        same = all(torch.equal(u, v) for u, v in zip(outputs, ys_p))
+        # the chain decodes the last wave of a multi-wave phase with half-size
+        # items (another summation order), so compare within fp32 rounding
+        diff = max(float((u - v).norm() / v.norm().clamp_min(1e-30)) for u, v in zip(outputs, ys_p))
         compare = {"independent_batch": {"us_per_step": round(batch_ms * 1e3, 1),
                                          "gbs": round(2.0 * weights_full / (batch_ms * 1e-3) / 1e9, 1),
                                          "how": "all projections as one independent batch "
                                                 "(rans_gemv_step_launch; ignores the phase order)"},
                    "per_phase_graph": {"us_per_step": round(graph_ms * 1e3, 1),
                                        "launches_per_step": sum(p.kernels for p in per_phase),
-                                       "outputs_identical_to_chain": bool(same),
+                                       "max_rel_l2_vs_chain": diff,
                                        "how": "one step launch per phase, captured in one CUDA graph"},
                    "chain_over_batch": round(t_ms / batch_ms, 3)}
         del g
         if check is not None:
-            check["chain_equals_per_phase_launches"] = bool(same)
-            check["ok"] = check["ok"] and bool(same)
+            check["chain_vs_per_phase_launches_max_rel_l2"] = diff
+            check["ok"] = check["ok"] and diff <= 1e-6
 
     # ---------------------------------------------------------------- e2e
     # through the public API: this step's activations from pinned host memory,

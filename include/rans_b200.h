@@ -134,15 +134,17 @@ int rans_gemv_step_kernels(const void* workspace);
  * i's phase; chunks of phase p start only after every chunk of phase p-1 has
  * finished (and, with `sync`, after every rank has signalled phase p-1).  The
  * table load and an L2 warm-up of the weights of a waiting chunk overlap the
- * previous phase.  Activations are read through L2, so phase p+1's x may be
- * phase p's y (the fp32 pre-scaled convention: step NULL) or a buffer written
- * by an earlier kernel.  No counterpart in the reference, whose harness
+ * previous phase.  Activations are read with coherent loads after the wait,
+ * so phase p+1's x may be phase p's y (the fp32 pre-scaled convention: step
+ * NULL).  A bf16 x (step given) must be written before the launch: the kernel
+ * turns it into fp32 x*step in the workspace one phase ahead of its use.  No counterpart in the reference, whose harness
  * launches one kernel per matrix (kernel/bench.py:104-107,
  * kernel/rans.py:147-151); this is the layer-level launcher of its survey.   */
 
 /* Row-sharded chain over the GPUs of one node (one process per GPU).
- * arrive: this rank's uint32[P] arrival counters in memory every rank can
- * write (NVLink peer mapping / symmetric memory); arrive_peer[r]: the address,
+ * arrive: this rank's uint32[P+1] arrival counters (the chain may add one
+ * phase in front of the caller's for activation prescaling) in memory every
+ * rank can write (NVLink peer mapping / symmetric memory); arrive_peer[r]: the address,
  * valid on this GPU, of rank r's counters (this rank included); peer_y as for
  * rans_gemv_step_plan_peers.  Every rank plans (which zeroes its counters),
  * then all ranks pass a host barrier, then every rank launches the same number
@@ -175,7 +177,8 @@ int rans_gemv_chain_launch(int R, const void* workspace, int grid, cudaStream_t 
 
 /* Synchronises `stream` and reports the chain's state: 0 when every wait of
  * the launches so far ended in time, -5 when one ran out (*phase_out = the
- * phase it waited for; outputs of that launch are incomplete).  Reading -5
+ * phase it waited for, -1 for the activation prescale in front of phase 0;
+ * outputs of that launch are incomplete).  Reading -5
  * clears it; until then launches return at once without work.  A multi-GPU
  * chain must then be planned again on every rank. */
 int rans_gemv_chain_status(void* workspace, int* phase_out, cudaStream_t stream);

@@ -1,10 +1,11 @@
 """The chain launcher (rans_gemv_chain_*): a decoder step as a chain of
 dependent phases from one persistent grid, through the C ABI.
 
-  * a 2-layer Qwen2.5-1.5B-shaped step (4 phases per layer) gives the same
-    outputs, bit for bit, as one step launch per phase (the planner gives each
-    phase the decomposition of a launch of its own) and matches the float64
-    oracle;
+  * a 2-layer Qwen2.5-1.5B-shaped step (4 phases per layer) gives the
+    outputs of one step launch per phase (the planner gives each phase the
+    decomposition of a launch of its own, up to half-size items in the last
+    wave of a multi-wave phase: equal within fp32 summation order) and matches
+    the float64 oracle;
   * phases that really feed each other (phase p+1's activation is phase p's
     output) read the finished output in every one of 20 back-to-back launches;
   * a dependency that never arrives (a second rank that does not exist, on
@@ -80,7 +81,9 @@ def test_chain_matches_one_launch_per_phase(torch, rb):
     chain.check()
     torch.cuda.synchronize()
     for a, b in zip(ys_chain, ys_step):
-        assert torch.equal(a, b)
+        # same decomposition except the chain's half-size items in the last
+        # wave of a multi-wave phase: equal up to fp32 summation order
+        assert float((a - b).norm() / b.norm()) <= 1e-6
     for y, x, (codes, step) in zip(ys_chain, xs, meta):
         _check_y(y.cpu().numpy(), orc.gemv(codes, step.astype(np.float64), x.float().cpu().numpy().astype(np.float64)))
 
@@ -123,11 +126,12 @@ def test_chain_wait_that_never_ends_reports_and_recovers(torch, rb):
     x = torch.randn(1536, generator=torch.Generator().manual_seed(3)).bfloat16().cuda()
     ys = [torch.empty(512, device="cuda") for _ in range(2)]
     dummy = [torch.zeros(512, device="cuda") for _ in range(2)]   # 'rank 1' output buffers
-    arrive = torch.zeros(2, dtype=torch.int32, device="cuda")
-    arrive_other = torch.zeros(2, dtype=torch.int32, device="cuda")  # nobody waits here
+    arrive = torch.zeros(4, dtype=torch.int32, device="cuda")
+    arrive_other = torch.zeros(4, dtype=torch.int32, device="cuda")  # nobody waits here
     peers = [[ys[i].data_ptr(), dummy[i].data_ptr()] for i in range(2)]
     sync = (2, 0, arrive.data_ptr(), [arrive.data_ptr(), arrive_other.data_ptr()], peers)
-    chain = rb.RansChain([m, m], [x, x], ys, [0, 1], timeout_ms=200, sync=sync)
+    xs = x.float() * torch.from_numpy(step).cuda()          # fp32 x*step: no prescale phase in front
+    chain = rb.RansChain([m, m], [xs, xs], ys, [0, 1], timeout_ms=200, sync=sync, prescaled_x=True)
     chain()
     with pytest.raises(rb.ChainTimeout) as e:
         chain.check()

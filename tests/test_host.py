@@ -169,3 +169,38 @@ def test_step_workspace_layout_without_gpu(lib):
     assert small_bf16 == small_f32
     assert lib.rans_gemv_step_workspace_bytes(_descs(1, 12, 1536, 512, True), 1, 8) == -2   # rows % R
     assert lib.rans_gemv_step_workspace_bytes(_descs(1, 256, 1536, 512, True), 1, 3) == -1  # bad R
+
+
+def test_chain_workspace_layout_without_gpu(lib):
+    """Host-side chain planning: phases must be numbered 0..P-1 without gaps;
+    the workspace holds the descriptors, the chunks of every phase, the phase
+    table and the control block, and never the prescaled activations (a
+    phase may read what the previous one wrote)."""
+    import ctypes
+    layer = [(1536, 1536, 512), (256, 1536, 512), (256, 1536, 512), (1536, 1536, 512),
+             (8960, 1536, 512), (8960, 1536, 512), (1536, 8960, 640)]
+    phase_of = [0, 0, 0, 1, 2, 2, 3]
+    for layers in (1, 4):
+        n = 7 * layers
+        arr = (rb.RansGemvDesc * n)()
+        for i in range(n):
+            rows, cols, C = layer[i % 7]
+            arr[i] = rb.RansGemvDesc(256, 256, 256, 256, 256, 256, 1 << 20, rows, cols, C, 0)
+        ph = (ctypes.c_int * n)(*[4 * (i // 7) + phase_of[i % 7] for i in range(n)])
+        b = lib.rans_gemv_chain_workspace_bytes(ctypes.addressof(arr), ctypes.addressof(ph), n, 8)
+        assert b > 0
+        if layers == 1:
+            one = b
+    assert b > 3 * one                                   # grows with the layers
+    bad = (ctypes.c_int * 7)(0, 0, 0, 2, 2, 2, 3)         # phase 1 missing
+    assert lib.rans_gemv_chain_workspace_bytes(ctypes.addressof(arr), ctypes.addressof(bad), 7, 8) == -2
+    neg = (ctypes.c_int * 7)(0, 0, 0, -1, 1, 1, 2)
+    assert lib.rans_gemv_chain_workspace_bytes(ctypes.addressof(arr), ctypes.addressof(neg), 7, 8) == -2
+    ok = (ctypes.c_int * 7)(*phase_of)
+    assert lib.rans_gemv_chain_workspace_bytes(ctypes.addressof(arr), ctypes.addressof(ok), 7, 3) == -1
+    # a bad timeout or rank description is refused before any CUDA call
+    assert lib.rans_gemv_chain_plan(ctypes.addressof(arr), ctypes.addressof(ok), 7, 8, None, 0, None, 0,
+                                    None, None) == -2
+    sync = rb.RansChainSync(9, 0, 256, 256, 256)
+    assert lib.rans_gemv_chain_plan(ctypes.addressof(arr), ctypes.addressof(ok), 7, 8, ctypes.addressof(sync),
+                                    1000, None, 0, None, None) == -2

@@ -27,6 +27,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <algorithm>
+#include <cmath>
 #include <cstddef>
 #include <mutex>
 #include <unordered_map>
@@ -191,21 +192,60 @@ __device__ __forceinline__ float entry_code(uint32_t e) {
 
 // Activation load mode XM: bit 0 set = bf16 x times the fp32 step (folded
 // here), clear = fp32 x already multiplied by the step; bit 1 set = load x
-// through L2 only (ld.global.cg), for kernels in which x may have been written
-// by other CTAs earlier in the same launch (the chain kernel: a phase's input
-// is an earlier phase's output), where the non-coherent path could return a
-// stale line.
-constexpr int kXBf16 = 1, kXCoherent = 2;
+// with plain (weak, L1-cached) global loads instead of the read-only path,
+// for kernels in which x may have been written by other CTAs earlier in the
+// same launch (the chain kernel: a phase's input is an earlier phase's
+// output).  There the CTA's reads follow an ld.acquire of the producer's
+// completion counter and a bar.sync, which the memory model extends to weak
+// loads; the non-coherent read-only path is outside it.
+// Bit 2 set = load the activations of k-step k+1 while k-step k decodes
+// (hides their latency where they miss L1: large activation vectors next to
+// 192 KB of shared memory per SM; the chain kernel uses it).
+// Bit 3 set = the chain kernel: before the first activation load each warp
+// waits for the previous phase (dep_wait) instead of the previous kernel.
+constexpr int kXBf16 = 1, kXCoherent = 2, kXPref = 4, kXChain = 8;
+
+// Per-CTA dependency state of the chain kernel, read inside the decode path:
+// the workspace header, the phase the current chunk waits for (-1: none) and,
+// per warp, the highest phase that warp has already seen complete.
+struct ChainHeader;
+__device__ bool chain_wait(const ChainHeader* h, int p);
+__shared__ const ChainHeader* g_chain_hdr;
+__shared__ int g_chain_wait;
+__shared__ int g_chain_known[kWarps];
+
+// Where the decode path may first touch activations: a step kernel waits for
+// the previous kernel of its stream (programmatic dependent launch), a chain
+// kernel's warp for the previous phase -- after its words are staged and its
+// states read, so both overlap the wait.  A chain wait that runs out has
+// recorded the error for the host; the warp then goes on (its outputs are
+// reported invalid) so the kernel always ends.
+template <int XM>
+__device__ __forceinline__ void dep_wait() {
+    if constexpr ((XM & kXChain) != 0) {
+        const int p = g_chain_wait;
+        const int w = threadIdx.x >> 5;
+        if (p >= 0 && p > g_chain_known[w]) {
+            int ok = 1;
+            if ((threadIdx.x & 31) == 0) ok = chain_wait(g_chain_hdr, p) ? 1 : 0;
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            if (ok && (threadIdx.x & 31) == 0) g_chain_known[w] = p;
+            __syncwarp();   // lane 0's acquire orders every lane's later loads
+        }
+    } else {
+        pdl_wait();
+    }
+}
 
 template <int XM>
 __device__ __forceinline__ float load_x(const MatDev& d, int c) {
     if (XM & kXBf16) {
         const unsigned short* xb = reinterpret_cast<const unsigned short*>(d.x);
-        const unsigned short v = (XM & kXCoherent) ? __ldcg(xb + c) : xb[c];
-        return __uint_as_float((uint32_t)v << 16) * __ldg(d.step + c);   // bf16 -> fp32 is exact
+        const uint32_t v = xb[c];   // plain load: never the read-only path
+        return __uint_as_float(v << 16) * __ldg(d.step + c);   // bf16 -> fp32 is exact
     } else {
         const float* xf = reinterpret_cast<const float*>(d.x);
-        return (XM & kXCoherent) ? __ldcg(xf + c) : __ldg(xf + c);
+        return (XM & kXCoherent) ? xf[c] : __ldg(xf + c);
     }
 }
 
@@ -400,12 +440,13 @@ __device__ __forceinline__ void decode_pass(const uint32_t (&pos)[K], const int 
         if (STAGED && RB_INNER != 0) p[j] += static_cast<uint32_t>(__cvta_generic_to_shared(g_smem));
     }
     const int nk = d.nk;
-    pdl_wait();   // activations may come from the previous kernel of the stream
+    dep_wait<XM>();   // activations may come from the previous kernel (or phase)
     float xn[K];
-    if (RB_XPREF) load_xs<K, NACC, XM>(d, xcol, kk, 0, xn);
+    constexpr bool kPref = RB_XPREF || (XM & kXPref);
+    if (kPref) load_xs<K, NACC, XM>(d, xcol, kk, 0, xn);
     for (int k = 0; k < nk; ++k) {
         float xv[K];
-        if (RB_XPREF) {
+        if (kPref) {
 #pragma unroll
             for (int j = 0; j < K; ++j) xv[j] = xn[j];
             if (k + 1 < nk) load_xs<K, NACC, XM>(d, xcol, kk, k + 1, xn);   // prefetch next k-step
@@ -488,7 +529,7 @@ __device__ __forceinline__ void decode_pass_windowed(uint32_t pos, const int (&x
     uint32_t p = pos + 2;                       // index of the next unread word (held in w)
     uint32_t w = __ldg(d.words + p);
     const int nk = d.nk;
-    pdl_wait();   // activations may come from the previous kernel of the stream
+    dep_wait<XM>();   // activations may come from the previous kernel (or phase)
     for (int k0 = 0; k0 < nk; k0 += kChunkK) {
         const uint32_t pw0 = refill_window(d, wgen, win, p, wend);
         uint32_t pw = pw0;
@@ -1713,7 +1754,7 @@ namespace rb200 {
 // increments the phase's completion counter.  The CTA that completes a phase
 // on a multi-GPU plan then adds 1 to that phase's arrival counter on every
 // rank (red.release.sys).  A waiting thread reads the counters with
-// ld.acquire, then bar.sync; activations are read through L2 (ld.global.cg).
+// ld.acquire, then bar.sync, then reads activations with weak L1-cached loads.
 //
 // The last CTA to leave resets the queue and completion counters and counts
 // the launch (epoch); arrival counters only grow, and a multi-GPU wait of
@@ -1724,10 +1765,13 @@ constexpr int32_t kChainTimeout = 1;
 
 struct ChainHeader {
     int ndesc, nchunks, R, nphases;
-    int npeer, rank, pad0, pad1;
+    int npeer, rank;
+    int shift;                 // kernel phase = caller phase + shift (1 when activations are prescaled up front)
+    int pad0;
     int64_t phase_off;         // int32 phase_end[nphases]: chunks [phase_end[p-1], phase_end[p]) are phase p
     int64_t ctl_off;           // ChainCtl, then uint32 done[nphases]
     int64_t timeout_ns;        // bound of every dependency wait
+    int64_t jobs_off;          // PrescaleJob[] of the activation prescale chunks
     uint32_t* arrive;          // this rank's arrival counters [nphases] (multi-GPU), or null
     uint32_t* arrive_peer[kMaxPeers];   // every rank's arrival counters, as addresses valid on this GPU
 };
@@ -1771,6 +1815,9 @@ __device__ __forceinline__ ChainCtl* chain_ctl(const ChainHeader* h) {
 __device__ __forceinline__ const int* chain_phase_end(const ChainHeader* h) {
     return reinterpret_cast<const int*>(reinterpret_cast<const uint8_t*>(h) + h->phase_off);
 }
+__device__ __forceinline__ const PrescaleJob* chain_jobs(const ChainHeader* h) {
+    return reinterpret_cast<const PrescaleJob*>(reinterpret_cast<const uint8_t*>(h) + h->jobs_off);
+}
 __device__ __forceinline__ const Chunk* chain_chunks(const ChainHeader* h) {
     return reinterpret_cast<const Chunk*>(reinterpret_cast<const MatDev*>(h + 1) + h->ndesc);
 }
@@ -1801,72 +1848,119 @@ __device__ bool chain_wait(const ChainHeader* h, int p) {
             return false;
         }
         __nanosleep(sleep_ns);
-        if (sleep_ns < 1024) sleep_ns *= 2;
+        if (sleep_ns < 256) sleep_ns *= 2;
+    }
+}
+
+// Chunk.phase of a chain chunk: the phase in the low bits; kChainAhead set
+// when at least a full wave of chunks of the same phase follows it, so the
+// CTA may take its next chunk while it works on this one (no CTA then holds
+// a chunk near a phase's end while busy with another).
+constexpr int kChainAhead = 1 << 30;
+constexpr int kChainPhaseMask = kChainAhead - 1;
+
+// Thread 0: the next chunk of the queue (nchunks once it is empty or an
+// error was reported).
+__device__ __forceinline__ int chain_grab(const ChainHeader* h) {
+    ChainCtl* ctl = chain_ctl(h);
+    if (*reinterpret_cast<volatile int32_t*>(&ctl->status) != 0) return h->nchunks;
+    return (int)min(atomicAdd(&ctl->queue, 1u), (uint32_t)h->nchunks);
+}
+
+// Thread 0: publish `count` finished chunks of phase p -- every output they
+// wrote (ordered before by the bar.sync that ended each chunk) is made
+// visible (fence; system scope when rows went to peers) and counted; the CTA
+// completing phase p on a multi-GPU plan tells every rank.  A CTA publishes
+// the chunks it finished in the middle of a phase together, when it moves to
+// another phase, reaches the phase's last wave or leaves (it never waits
+// while holding unpublished chunks, and the fence is paid rarely); chunks of
+// a phase's last wave are published as soon as they end.
+__device__ __forceinline__ void chain_signal(const ChainHeader* h, int p, uint32_t count) {
+    uint32_t* done = reinterpret_cast<uint32_t*>(chain_ctl(h) + 1);
+    if (h->npeer > 0) {
+        __threadfence_system();
+        const uint32_t prev = atomicAdd(done + p, count);
+        if (prev + count == phase_chunks(chain_phase_end(h), p))
+            for (int q = 0; q < h->npeer; ++q) red_release_sys(h->arrive_peer[q] + p, 1u);
+    } else {
+        __threadfence();
+        atomicAdd(done + p, count);
     }
 }
 
 template <int R>
 __global__ void __launch_bounds__(kThreads, RB_MINB) gemv_chain_kernel(const ChainHeader* __restrict__ hdr) {
-    __shared__ int s_chunk, s_go;
+    __shared__ int s_chunk;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const SmemMap sm = smem_map(warp);
-    int cur = -1;   // matrix whose table is in shared memory
+    const uint32_t* cur = nullptr;    // table now in shared memory
+    int next = -1;                    // thread 0: chunk taken ahead, or -1
+    int pend_phase = -1;              // thread 0: phase of finished, unpublished chunks
+    uint32_t pend = 0;                //           and how many
+    if (threadIdx.x == 0) {
+        g_chain_hdr = hdr;
+        s_chunk = chain_grab(hdr);
+    }
+    if (lane == 0) g_chain_known[warp] = -1;
+    __syncthreads();
     for (;;) {
-        if (threadIdx.x == 0) {
-            ChainCtl* ctl = chain_ctl(hdr);
-            int c = hdr->nchunks;
-            if (*reinterpret_cast<volatile int32_t*>(&ctl->status) == 0) c = (int)atomicAdd(&ctl->queue, 1u);
-            s_chunk = c;
-        }
-        __syncthreads();
         const int c = s_chunk;
         if (c >= hdr->nchunks) break;
         const Chunk ch = chain_chunks(hdr)[c];
-        const MatDev& d = reinterpret_cast<const MatDev*>(hdr + 1)[ch.desc];
-        // weights are immutable: the table load and the L2 warm-up of the
-        // chunk's words overlap the wait for the previous phase
-        if (ch.desc != cur) {
-            load_table(sm.tab, d.table);
-            cur = ch.desc;
-        }
+        const int phase = ch.phase & kChainPhaseMask;
         if (threadIdx.x == 0) {
-            int go = 1;
-            if (ch.phase > 0) {
-                int64_t t0, t1, u0, u1;
-                item_tiles(d, ch.item0, t0, t1);
-                item_tiles(d, ch.item0 + ch.nitems - 1, u0, u1);
-                const uint32_t w0 = d.offs[t0 * 32];
-                const uint64_t w1 = span_end(d, u1 * 32);
-                if (w1 != UINT64_MAX && w1 > w0) prefetch_l2(d.words + w0, 2ull * (w1 - w0));
-                go = chain_wait(hdr, ch.phase - 1) ? 1 : 0;
+            if (pend > 0 && pend_phase != phase) {
+                chain_signal(hdr, pend_phase, pend);   // before any wait of this chunk
+                pend = 0;
             }
-            s_go = go;
+            if (ch.phase & kChainAhead) next = chain_grab(hdr);   // used at the end of this chunk
         }
-        __syncthreads();
-        if (!s_go) break;
-        if (warp < ch.nitems) {
-            int bad = 0;
-            const MatDev dl = d;
-            if (dl.step != nullptr)
-                process_item<R, kXBf16 | kXCoherent>(dl, ch.item0 + warp, sm.tab, sm.stage, lane, bad, warp, ch.nitems);
-            else
-                process_item<R, kXCoherent>(dl, ch.item0 + warp, sm.tab, sm.stage, lane, bad, warp, ch.nitems);
-        }
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            const int p = chain_chunks(hdr)[s_chunk].phase;
-            if (hdr->npeer > 0) __threadfence_system();
-            else __threadfence();
-            uint32_t* done = reinterpret_cast<uint32_t*>(chain_ctl(hdr) + 1);
-            const uint32_t prev = atomicAdd(done + p, 1u);
-            if (hdr->npeer > 0 && prev + 1 == phase_chunks(chain_phase_end(hdr), p)) {
-                // this GPU's rows of the phase are everywhere: tell every rank
-                for (int q = 0; q < hdr->npeer; ++q) red_release_sys(hdr->arrive_peer[q] + p, 1u);
+        if (ch.nitems < 0) {
+            // activation prescale job: x' = bf16 x * step for columns
+            // [item0, item0 - nitems) of one matrix, read by the next phase.
+            // Its inputs were written before the launch: no wait.
+            const PrescaleJob jb = chain_jobs(hdr)[ch.desc];
+            const unsigned short* xb = reinterpret_cast<const unsigned short*>(jb.x);
+            for (int col = ch.item0 + (int)threadIdx.x; col < ch.item0 - ch.nitems; col += blockDim.x)
+                jb.out[col] = __uint_as_float((uint32_t)xb[col] << 16) * __ldg(jb.step + col);
+        } else {
+            const MatDev& d = reinterpret_cast<const MatDev*>(hdr + 1)[ch.desc];
+            // weights are immutable: the table load and each warp's staging
+            // and state reads overlap the previous phase; each warp waits for
+            // it only before its first activation load (dep_wait)
+            if (d.table != cur) {
+                load_table(sm.tab, d.table);
+                cur = d.table;
+            }
+            if (threadIdx.x == 0) g_chain_wait = phase > 0 ? phase - 1 : -1;
+            __syncthreads();
+            if (warp < ch.nitems) {
+                // every activation is fp32 x*step here (the planner turned bf16
+                // ones into prescale jobs of the previous phase)
+                int bad = 0;
+                const MatDev dl = d;
+                process_item<R, kXCoherent | kXPref | kXChain>(dl, ch.item0 + warp, sm.tab, sm.stage, lane, bad,
+                                                                warp, ch.nitems);
             }
         }
+        __syncthreads();   // every output of chunk c is written
+        if (threadIdx.x == 0) {
+            pend_phase = phase;
+            ++pend;
+            if (!(ch.phase & kChainAhead)) {
+                // one of the phase's last chunks: its completion may be what
+                // the next phase waits for, publish it now
+                chain_signal(hdr, phase, pend);
+                pend = 0;
+            }
+            s_chunk = next >= 0 ? next : chain_grab(hdr);
+            next = -1;
+        }
+        __syncthreads();
     }
-    // the last CTA out resets the queue and the completion counters
     if (threadIdx.x == 0) {
+        if (pend > 0) chain_signal(hdr, pend_phase, pend);
+        // the last CTA out resets the queue and the completion counters
         ChainCtl* ctl = chain_ctl(hdr);
         __threadfence();
         const uint32_t n = atomicAdd(&ctl->exited, 1u);
@@ -1883,12 +1977,26 @@ __global__ void __launch_bounds__(kThreads, RB_MINB) gemv_chain_kernel(const Cha
 
 struct ChainLayout {
     std::vector<MatDev> mats;
-    std::vector<int> phase_end;    // per phase: one past its last chunk
-    int nphases = 0;
-    int64_t nchunks = 0;
-    size_t phase_off = 0, ctl_off = 0, counters_off = 0, partials_off = 0, bytes = 0;
+    std::vector<PrescaleJob> jobs;     // activation prescale jobs (out set when planned into a workspace)
+    std::vector<int> job_mat;          // the matrix of each job
+    std::vector<int> parent;           // per decomposition: the caller's matrix it belongs to
+    std::vector<int> head_rb;          // per decomposition split in two: first row block of the fine tail
+    std::vector<size_t> xprime;        // per matrix: byte offset of its x' (0 = fp32 x given)
+    std::vector<Chunk> chunks;         // in hand-out order
+    std::vector<int> phase_end;        // per kernel phase: one past its last chunk
+    int nphases = 0;                   // kernel phases (the caller's, plus one in front when needed)
+    int shift = 0;                     // 1 when that front phase (activation prescale) exists
+    size_t jobs_off = 0, phase_off = 0, ctl_off = 0, counters_off = 0, partials_off = 0, xprime_off = 0,
+           bytes = 0;
 };
 
+constexpr int kPrescaleCols = 8192;    // columns per activation prescale chunk
+
+// The chain's work list.  Caller phase p becomes kernel phase p + shift; a
+// matrix with bf16 activations (written before the launch) reads a prescaled
+// fp32 copy x' that prescale chunks of the kernel phase before its own write
+// (for caller phase 0 that is an extra kernel phase 0, shift = 1).  Within a
+// phase: its prescale chunks first, then its decode chunks, longest first.
 static int layout_chain(const RansGemvDesc* descs, const int* phase, int n, int R, ChainLayout& L) {
     if (n <= 0 || descs == nullptr || phase == nullptr) return -2;
     int P = 0;
@@ -1903,25 +2011,132 @@ static int layout_chain(const RansGemvDesc* descs, const int* phase, int n, int 
     L.mats.clear();
     if (count_chunks(descs, n, R, &L.mats) < 0) return -2;
     int64_t ncounters = 0, npartials = 0;
-    L.phase_end.assign(P, 0);
-    L.nphases = P;
-    L.nchunks = 0;
+    L.parent.resize(n);
+    for (int i = 0; i < n; ++i) L.parent[i] = i;
+    L.head_rb.assign(n, -1);
+    std::vector<std::vector<int>> tails(P);     // per phase: the fine decompositions (indices into mats)
+    const int64_t W = split_target();
     for (int p = 0; p < P; ++p) {
         // each phase runs on the whole GPU by itself: plan it like one launch
         std::vector<MatDev> g;
         for (int i : members[p]) g.push_back(L.mats[i]);
         plan_group(g, R, ncounters, npartials);
+        int64_t items = 0;
         for (size_t k = 0; k < g.size(); ++k) {
             L.mats[members[p][k]] = g[k];
-            L.nchunks += (g[k].nitems + chunk_items(g[k]) - 1) / chunk_items(g[k]);
+            items += g[k].nitems;
         }
-        L.phase_end[p] = (int)L.nchunks;
+        if (items <= W) continue;
+        // A phase of several waves ends in a partly filled last wave of whole
+        // items, and the next phase cannot start before it ends.  Its last
+        // wave's worth of row blocks (about W / items of every matrix) is
+        // therefore decoded as items of half as many tiles (one pass each),
+        // handed out after everything else: a second decomposition of the
+        // same matrix covering the tail's row blocks only (its chunks select
+        // those items).  (One-tile items measured slower: their staging,
+        // reduction and global partial sums cost more than the tail saved.)
+        const double f = std::min(0.5, (double)W / (double)items);
+        for (int i : members[p]) {
+            const MatDev& d = L.mats[i];
+            int kf = 0;
+            for (int t = d.cbs / 2; t >= 1 && kf == 0; --t)
+                if (d.ncb % t == 0) kf = t;
+            if (kf == 0 || kf >= d.kcol) continue;            // nothing finer with fewer streams
+            const int tail = std::min(d.nrb, std::max(1, (int)std::ceil(f * d.nrb)));
+            MatDev fd = d;
+            fd.kcol = kf;
+            fd.nseg = d.ncb / kf;
+            fd.cbs = kf;
+            fd.nitems = d.nrb * fd.nseg;
+            fd.accumulate = 0;
+            fd.combine = fd.nseg <= kWarps ? 1 : 0;
+            fd.counters = nullptr;
+            fd.partials = nullptr;
+            if (!fd.combine) {
+                ncounters += fd.nrb;
+                npartials += (int64_t)fd.nrb * fd.nseg * R;
+            }
+            L.head_rb[i] = d.nrb - tail;
+            L.mats.push_back(fd);
+            L.parent.push_back(i);
+            L.head_rb.push_back(d.nrb - tail);             // the fine one starts there
+            tails[p].push_back((int)L.mats.size() - 1);
+        }
     }
-    L.phase_off = align16(sizeof(ChainHeader) + sizeof(MatDev) * (size_t)n + sizeof(Chunk) * (size_t)L.nchunks);
-    L.ctl_off = align16(L.phase_off + sizeof(int) * (size_t)P);
-    L.counters_off = align16(L.ctl_off + sizeof(ChainCtl) + sizeof(uint32_t) * (size_t)P);
+    // prescale jobs and x' buffers of the bf16-activation matrices
+    L.jobs.clear();
+    L.job_mat.clear();
+    L.xprime.assign(n, 0);
+    std::vector<int> job_of(n, -1);
+    size_t xbytes = 0;
+    for (int i = 0; i < n; ++i) {
+        if (L.mats[i].step == nullptr) continue;
+        job_of[i] = (int)L.jobs.size();
+        PrescaleJob jb;
+        jb.x = static_cast<const __nv_bfloat16*>(L.mats[i].x);
+        jb.step = L.mats[i].step;
+        jb.out = nullptr;
+        jb.cols = L.mats[i].cols;
+        jb.pad_ = 0;
+        L.jobs.push_back(jb);
+        L.job_mat.push_back(i);
+        L.xprime[i] = xbytes;              // relative to xprime_off until the offsets are known
+        xbytes = align16(xbytes + sizeof(float) * (size_t)L.mats[i].cols);
+    }
+    auto prescale_chunks = [&](int p, int kphase) {
+        for (int i : members[p]) {
+            if (job_of[i] < 0) continue;
+            for (int c0 = 0; c0 < L.mats[i].cols; c0 += kPrescaleCols) {
+                const int cnt = std::min(kPrescaleCols, L.mats[i].cols - c0);
+                L.chunks.push_back(Chunk{job_of[i], c0, -cnt, kphase});
+            }
+        }
+    };
+    auto item_cost = [&](const MatDev& d) -> int64_t { return (int64_t)R * d.cbs * d.C; };
+    bool front = false;
+    for (int i : members[0]) front = front || job_of[i] >= 0;
+    const int shift = front ? 1 : 0;
+    L.chunks.clear();
+    L.phase_end.clear();
+    if (front) {
+        prescale_chunks(0, 0);
+        L.phase_end.push_back((int)L.chunks.size());
+    }
+    for (int p = 0; p < P; ++p) {
+        const int kp = p + shift;
+        if (p + 1 < P) prescale_chunks(p + 1, kp);
+        // items [i0, i1) of decomposition k (row blocks split at head_rb)
+        auto emit = [&](int k, int i0, int i1) {
+            const int cs = chunk_items(L.mats[k]);
+            for (int it = i0; it < i1; it += cs) L.chunks.push_back(Chunk{k, it, std::min(cs, i1 - it), kp});
+        };
+        auto by_cost = [&](size_t c0) {
+            // longest chunks first: the last CTAs to start run the shortest
+            std::stable_sort(L.chunks.begin() + c0, L.chunks.end(), [&](const Chunk& a, const Chunk& b) {
+                return item_cost(L.mats[a.desc]) > item_cost(L.mats[b.desc]);
+            });
+        };
+        size_t c0 = L.chunks.size();
+        for (int i : members[p]) {
+            const MatDev& d = L.mats[i];
+            emit(i, 0, L.head_rb[i] < 0 ? d.nitems : L.head_rb[i] * d.nseg);
+        }
+        by_cost(c0);
+        c0 = L.chunks.size();
+        for (int k : tails[p]) emit(k, L.head_rb[k] * L.mats[k].nseg, L.mats[k].nitems);
+        by_cost(c0);
+        L.phase_end.push_back((int)L.chunks.size());
+    }
+    L.nphases = P + shift;
+    L.shift = shift;
+    const size_t nch = L.chunks.size();
+    L.jobs_off = align16(sizeof(ChainHeader) + sizeof(MatDev) * L.mats.size() + sizeof(Chunk) * nch);
+    L.phase_off = align16(L.jobs_off + sizeof(PrescaleJob) * L.jobs.size());
+    L.ctl_off = align16(L.phase_off + sizeof(int) * (size_t)L.nphases);
+    L.counters_off = align16(L.ctl_off + sizeof(ChainCtl) + sizeof(uint32_t) * (size_t)L.nphases);
     L.partials_off = align16(L.counters_off + sizeof(uint32_t) * (size_t)ncounters);
-    L.bytes = align16(L.partials_off + sizeof(float) * (size_t)npartials);
+    L.xprime_off = align16(L.partials_off + sizeof(float) * (size_t)npartials);
+    L.bytes = L.xprime_off + xbytes;
     return 0;
 }
 
@@ -1965,13 +2180,20 @@ extern "C" int rans_gemv_chain_plan(const RansGemvDesc* descs, const int* phase,
     if (L.bytes > workspace_bytes) return -3;
     uint8_t* ws = static_cast<uint8_t*>(workspace);
     int64_t coff = 0, poff = 0;
-    for (int i = 0; i < n; ++i) {
-        MatDev& d = L.mats[i];
+    const int nm = (int)L.mats.size();     // the caller's matrices, then the fine tails
+    for (int k = 0; k < nm; ++k) {
+        MatDev& d = L.mats[k];
+        const int i = L.parent[k];
         if (d.nseg > 1 && !d.accumulate && !d.combine) {
             d.counters = reinterpret_cast<uint32_t*>(ws + L.counters_off) + coff;
             d.partials = reinterpret_cast<float*>(ws + L.partials_off) + poff;
             coff += d.nrb;
             poff += (int64_t)d.nrb * d.nseg * R;
+        }
+        if (d.step != nullptr) {
+            // decode reads the prescaled copy written by the prescale chunks
+            d.x = ws + L.xprime_off + L.xprime[i];
+            d.step = nullptr;
         }
         if (sync != nullptr) {
             if (d.accumulate) return -2;   // atomically accumulated rows cannot be exchanged by stores
@@ -1980,12 +2202,14 @@ extern "C" int rans_gemv_chain_plan(const RansGemvDesc* descs, const int* phase,
                 d.ypeer[p] = static_cast<float*>(const_cast<void*>(sync->peer_y[(size_t)i * sync->nranks + p]));
         }
     }
-    // host image up to the partials (header, descriptors, chunks, phase ends,
-    // zeroed control block and segment counters)
+    for (size_t j = 0; j < L.jobs.size(); ++j)
+        L.jobs[j].out = reinterpret_cast<float*>(ws + L.xprime_off + L.xprime[L.job_mat[j]]);
+    // host image up to the partials (header, descriptors, chunks, prescale
+    // jobs, phase ends, zeroed control block and segment counters)
     std::vector<uint8_t> host(L.partials_off, 0);
     ChainHeader* h = reinterpret_cast<ChainHeader*>(host.data());
-    h->ndesc = n;
-    h->nchunks = (int)L.nchunks;
+    h->ndesc = nm;
+    h->nchunks = (int)L.chunks.size();
     h->R = R;
     h->nphases = L.nphases;
     h->npeer = sync ? sync->nranks : 0;
@@ -1993,37 +2217,27 @@ extern "C" int rans_gemv_chain_plan(const RansGemvDesc* descs, const int* phase,
     h->phase_off = (int64_t)L.phase_off;
     h->ctl_off = (int64_t)L.ctl_off;
     h->timeout_ns = (int64_t)timeout_ms * 1000000ll;
+    h->jobs_off = (int64_t)L.jobs_off;
+    h->shift = L.shift;
     if (sync) {
         h->arrive = static_cast<uint32_t*>(sync->arrive);
         for (int p = 0; p < sync->nranks; ++p) h->arrive_peer[p] = static_cast<uint32_t*>(sync->arrive_peer[p]);
     }
     MatDev* md = reinterpret_cast<MatDev*>(h + 1);
-    Chunk* ch = reinterpret_cast<Chunk*>(md + n);
-    for (int i = 0; i < n; ++i) md[i] = L.mats[i];
-    int64_t c = 0;
-    auto item_cost = [&](const MatDev& d) -> int64_t { return (int64_t)R * d.cbs * d.C; };
-    for (int p = 0; p < L.nphases; ++p) {
-        const int64_t c0 = c;
-        for (int i = 0; i < n; ++i) {
-            if (phase[i] != p) continue;
-            const int cs = chunk_items(md[i]);
-            for (int it = 0; it < md[i].nitems; it += cs) {
-                ch[c].desc = i;
-                ch[c].item0 = it;
-                ch[c].nitems = md[i].nitems - it < cs ? md[i].nitems - it : cs;
-                ch[c].phase = p;
-                ++c;
-            }
-        }
-        // longest chunks of the phase first: its last CTAs to start run the shortest
-        std::stable_sort(ch + c0, ch + c, [&](const Chunk& a, const Chunk& b) {
-            return item_cost(md[a.desc]) > item_cost(md[b.desc]);
-        });
-    }
+    for (int k = 0; k < nm; ++k) md[k] = L.mats[k];
+    std::memcpy(md + nm, L.chunks.data(), sizeof(Chunk) * L.chunks.size());
+    if (!L.jobs.empty()) std::memcpy(host.data() + L.jobs_off, L.jobs.data(), sizeof(PrescaleJob) * L.jobs.size());
     int* pe = reinterpret_cast<int*>(host.data() + L.phase_off);
     for (int p = 0; p < L.nphases; ++p) pe[p] = L.phase_end[p];
-    const int grid = chain_grid(R, L.nchunks);
+    const int grid = chain_grid(R, (int64_t)L.chunks.size());
     if (grid <= 0) return (int)cudaErrorInvalidConfiguration;
+    {
+        // chunks followed by at least a full wave of their own phase may be
+        // taken one chunk ahead
+        Chunk* chw = reinterpret_cast<Chunk*>(md + nm);
+        for (size_t c = 0; c < L.chunks.size(); ++c)
+            if ((int64_t)c + grid < L.phase_end[chw[c].phase]) chw[c].phase |= kChainAhead;
+    }
     cudaError_t e = cudaMemcpyAsync(workspace, host.data(), host.size(), cudaMemcpyHostToDevice, stream);
     if (e != cudaSuccess) return (int)e;
     if (sync != nullptr) {
@@ -2070,7 +2284,8 @@ extern "C" int rans_gemv_chain_status(void* workspace, int* phase_out, cudaStrea
     e = cudaMemcpyAsync(&ctl, ctl_dev, sizeof(ctl), cudaMemcpyDeviceToHost, stream);
     if (e != cudaSuccess) return (int)e;
     if ((e = cudaStreamSynchronize(stream)) != cudaSuccess) return (int)e;
-    if (phase_out) *phase_out = ctl.status != 0 ? ctl.where : -1;
+    // the caller's phase (kernel phases count an up-front prescale phase)
+    if (phase_out) *phase_out = ctl.status != 0 ? ctl.where - h.shift : -1;
     if (ctl.status == 0) return 0;
     // read and cleared: the next launch runs again
     e = cudaMemsetAsync(ctl_dev + offsetof(ChainCtl, status), 0, 2 * sizeof(int32_t), stream);

@@ -227,7 +227,9 @@ class ShardedChain:
         self.y_full = symm_mem.empty(self.layout.total, dtype=torch.float32, device=dev)
         self.y_full.zero_()
         self.hdl = _symm_rendezvous(self.y_full)
-        self.arrive = symm_mem.empty(max(nphases, 4), dtype=torch.int32, device=dev)
+        # one more than the caller's phases: the chain may add an activation
+        # prescale phase in front
+        self.arrive = symm_mem.empty(max(nphases + 1, 4), dtype=torch.int32, device=dev)
         self.arrive.zero_()
         self.hdl_arrive = _symm_rendezvous(self.arrive)
         peers = self.layout.peer_addresses([int(p) for p in self.hdl.buffer_ptrs], self.rank)
