@@ -70,12 +70,22 @@ constexpr int kPadWords = 8;
 #ifndef RB_ALIGNTAB
 #define RB_ALIGNTAB 1    // place the table at a 16 KB-aligned shared address (address = one LOP3)
 #endif
+#ifndef RB_TABCOPIES
+#define RB_TABCOPIES 2   // copies of the slot table in shared memory, interleaved by lane (1 or 2)
+#endif
+// The table sits at an aligned address (entry address = shift + one LOP3)
+// only with one copy; two lane-interleaved copies (entry of slot s for lane l
+// at word 2s + (l & 1): the lanes of one parity reach only every other bank)
+// use and + shift-add at any address.
+#define RB_TAB_ALIGNED (RB_ALIGNTAB && RB_TABCOPIES == 1)
 constexpr int kWarps = RB_WARPS;          // warps per CTA
 constexpr int kI4Unroll = RB_I4_UNROLL;
 constexpr int kThreads = kWarps * 32;
 constexpr int kStageBytes = RB_STAGE_BYTES;  // per-warp staging buffer (0: no staging)
-constexpr int kTableBytes = kProbM * 4;
-constexpr int kAlignPad = RB_ALIGNTAB ? kTableBytes : 0;
+constexpr int kTabCopies = RB_TABCOPIES;
+static_assert(kTabCopies == 1 || kTabCopies == 2, "one or two table copies");
+constexpr int kTableBytes = kProbM * 4 * kTabCopies;     // in shared memory
+constexpr int kAlignPad = RB_TAB_ALIGNED ? kTableBytes : 0;
 constexpr int kSmemBytes = kTableBytes + kWarps * kStageBytes + kAlignPad;
 // Layout 1 yields 4096*code from one LOP3; the sums are scaled back by 2^-12 (exact).
 constexpr float kCodeScale = RB_LAYOUT == 1 ? 4096.0f : 1.0f;
@@ -134,7 +144,7 @@ struct SmemMap {
 __device__ __forceinline__ SmemMap smem_map(int warp) {
     SmemMap m;
     const uint32_t base = static_cast<uint32_t>(__cvta_generic_to_shared(g_smem));
-    const uint32_t toff = RB_ALIGNTAB ? ((uint32_t)kTableBytes - (base & (kTableBytes - 1))) & (kTableBytes - 1) : 0u;
+    const uint32_t toff = RB_TAB_ALIGNED ? ((uint32_t)kTableBytes - (base & (kTableBytes - 1))) & (kTableBytes - 1) : 0u;
     m.tab = reinterpret_cast<uint32_t*>(g_smem + toff);
     m.tab_s = base + toff;
     const int nbefore = kStageBytes > 0 ? (int)(toff / kStageBytes) : 0;
@@ -171,7 +181,20 @@ __device__ __forceinline__ uint32_t relayout_entry(uint32_t e) {
 }
 
 __device__ __forceinline__ void load_table(uint32_t* tab, const uint32_t* __restrict__ table) {
-    for (int i = threadIdx.x; i < (int)kProbM; i += blockDim.x) tab[i] = relayout_entry(__ldg(table + i));
+    for (int i = threadIdx.x; i < (int)kProbM; i += blockDim.x) {
+        const uint32_t e = relayout_entry(__ldg(table + i));
+#pragma unroll
+        for (int c = 0; c < kTabCopies; ++c) tab[i * kTabCopies + c] = e;
+    }
+}
+
+// The table entry of a state for this thread's lane (C++ paths), and the
+// shared address the PTX paths add the slot offset to.
+__device__ __forceinline__ uint32_t tab_entry(const uint32_t* tab, uint32_t st) {
+    return tab[(st & (kProbM - 1)) * kTabCopies + (threadIdx.x & (kTabCopies - 1))];
+}
+__device__ __forceinline__ uint32_t tab_lane_base(uint32_t tab_s) {
+    return tab_s + 4u * (threadIdx.x & (kTabCopies - 1));
 }
 
 __device__ __forceinline__ uint32_t entry_freq(uint32_t e) { return e >> 20; }
@@ -401,7 +424,16 @@ __device__ __forceinline__ void load_xs(const MatDev& d, const int (&xcol)[K], i
 // single immediate: (e & 0xff000) | magic).
 __device__ __forceinline__ void sym_step_ptx(uint32_t& st, uint32_t& w, uint32_t& pw, float& acc, float xv,
                                              uint32_t tb, uint32_t magic) {
-#if RB_ALIGNTAB
+#if RB_TABCOPIES == 2
+    // two lane-interleaved copies: tb is this lane's copy (table + 4 * (lane & 1))
+    asm("{\n\t.reg .pred p;\n\t.reg .b32 e, f, b, hi, a, c;\n\t"
+        "and.b32 a, %0, 4095;\n\t"
+        "shl.b32 a, a, 3;\n\t"
+        "add.u32 a, a, %5;\n\t"
+        "ld.shared.u32 e, [a];\n\t" RB_PTX_FIELDS
+        : "+r"(st), "+r"(w), "+r"(pw), "+f"(acc)
+        : "f"(xv), "r"(tb), "r"(magic));
+#elif RB_ALIGNTAB
     asm("{\n\t.reg .pred p;\n\t.reg .b32 e, f, b, hi, a, c;\n\t"
         "shl.b32 a, %0, 2;\n\t"
         "and.b32 a, a, 0x3FFC;\n\t"
@@ -428,7 +460,7 @@ __device__ __forceinline__ void decode_pass(const uint32_t (&pos)[K], const int 
     // a shuffle result: the compiler cannot fold it back into an immediate
     const uint32_t magic = __shfl_sync(0xffffffffu, 0x4B000000u, 0);
     const uint32_t* tab = sm.tab;
-    const uint32_t tb = sm.tab_s;
+    const uint32_t tb = tab_lane_base(sm.tab_s);
     uint32_t st[K], w[K], p[K];
 #pragma unroll
     for (int j = 0; j < K; ++j) {
@@ -462,7 +494,7 @@ __device__ __forceinline__ void decode_pass(const uint32_t (&pos)[K], const int 
                     sym_step_ptx(st[j], w[j], p[j], a, xv[j], tb, magic);
                     continue;
                 }
-                const uint32_t e = tab[st[j] & (kProbM - 1)];
+                const uint32_t e = tab_entry(tab, st[j]);
                 st[j] = entry_freq(e) * (st[j] >> kScaleBits) + entry_bias(e);
                 if (st[j] < kRansL) {
                     st[j] = __byte_perm(w[j], st[j], 0x5410);
@@ -517,10 +549,10 @@ __device__ __forceinline__ void decode_pass_windowed(uint32_t pos, const int (&x
                                                   uint64_t limit) {
     constexpr int kChunkK = (kWinWords - 8) / R;   // head <= 7 words, then <= 1 word per symbol
     static_assert(kChunkK >= 1, "stage too small for windowed staging");
-    static_assert(RB_LAYOUT == 1 && RB_ALIGNTAB, "windowed passes use the PTX symbol step");
+    static_assert(RB_LAYOUT == 1 && (RB_ALIGNTAB || RB_TABCOPIES == 2), "windowed passes use the PTX symbol step");
     const SmemMap sm = smem_map(0);
     const uint32_t magic = __shfl_sync(0xffffffffu, 0x4B000000u, 0);
-    const uint32_t tb = sm.tab_s;
+    const uint32_t tb = tab_lane_base(sm.tab_s);
     uint8_t* const wgen = reinterpret_cast<uint8_t*>(stage) + lane * kWinBytes;   // this lane's window
     const uint32_t win = static_cast<uint32_t>(__cvta_generic_to_shared(wgen));
     const uintptr_t wbase = reinterpret_cast<uintptr_t>(d.words);
@@ -764,7 +796,7 @@ __device__ __forceinline__ void prefetch_next_chunk(const StepHeader* hdr, const
     const uint2 sp = reinterpret_cast<const uint2*>(reinterpret_cast<const uint8_t*>(hdr) + hdr->spans_off)[nb];
     const MatDev& dn = descs[chunks[nb].desc];
     if (sp.y > sp.x) prefetch_l2(dn.words + sp.x, 2ull * (sp.y - sp.x));
-    prefetch_l2(dn.table, kTableBytes);
+    prefetch_l2(dn.table, kProbM * 4);
 }
 
 // Every projection of a decoder step: CTA b processes chunk b (one matrix).
@@ -793,13 +825,19 @@ __global__ void __launch_bounds__(kThreads, RB_MINB) gemv_step_kernel(const Step
 // decode-to-dense path.  Same sequence as sym_step_ptx.
 __device__ __forceinline__ float sym_code(uint32_t& st, uint32_t& w, uint32_t& pw, uint32_t tb, const uint32_t* tab,
                                           bool staged, const MatDev& d, uint32_t magic) {
-#if RB_LAYOUT == 1 && RB_ALIGNTAB
+#if RB_LAYOUT == 1 && (RB_ALIGNTAB || RB_TABCOPIES == 2)
     if (staged) {
         float c;
         asm("{\n\t.reg .pred p;\n\t.reg .b32 e, f, b, hi, a, t;\n\t"
+#if RB_TABCOPIES == 2
+            "and.b32 a, %0, 4095;\n\t"
+            "shl.b32 a, a, 3;\n\t"
+            "add.u32 a, a, %4;\n\t"
+#else
             "shl.b32 a, %0, 2;\n\t"
             "and.b32 a, a, 0x3FFC;\n\t"
             "or.b32 a, a, %4;\n\t"
+#endif
             "ld.shared.u32 e, [a];\n\t"
             "shr.u32 f, e, 20;\n\t"
             "and.b32 b, e, 4095;\n\t"
@@ -816,7 +854,7 @@ __device__ __forceinline__ float sym_code(uint32_t& st, uint32_t& w, uint32_t& p
         return c;
     }
 #endif
-    const uint32_t e = tab[st & (kProbM - 1)];
+    const uint32_t e = tab_entry(tab, st);
     st = entry_freq(e) * (st >> kScaleBits) + entry_bias(e);
     if (st < kRansL) {
         st = __byte_perm(w, st, 0x5410);
@@ -835,7 +873,7 @@ template <int R, int K, bool STAGED>
 __device__ __forceinline__ void decode_store(const MatDev& d, const uint32_t (&pos)[K], int kk,
                                              __nv_bfloat16* const (&orow)[K], const int (&col0)[K]) {
     const SmemMap sm = smem_map(0);
-    const bool ptx = STAGED && RB_LAYOUT == 1 && RB_ALIGNTAB;
+    const bool ptx = STAGED && RB_LAYOUT == 1 && (RB_ALIGNTAB || RB_TABCOPIES == 2);
     const uint32_t sbase = static_cast<uint32_t>(__cvta_generic_to_shared(g_smem));
     uint32_t st[K], w[K], p[K];
 #pragma unroll
@@ -872,10 +910,10 @@ __device__ __forceinline__ void decode_store(const MatDev& d, const uint32_t (&p
             for (int j = 0; j < K; ++j) {
                 float c;
                 if (ptx) {
-                    c = sym_code(st[j], w[j], p[j], sm.tab_s, sm.tab, true, d, magic);
+                    c = sym_code(st[j], w[j], p[j], tab_lane_base(sm.tab_s), sm.tab, true, d, magic);
                 } else {
                     // generic pointer bookkeeping of the C++ step uses offsets from g_smem
-                    c = sym_code(st[j], w[j], p[j], sm.tab_s, sm.tab, STAGED, d, magic);
+                    c = sym_code(st[j], w[j], p[j], tab_lane_base(sm.tab_s), sm.tab, STAGED, d, magic);
                 }
                 // no branch on j < kk: a slot past kk replays tile kk-1 and
                 // stores the same values to the same place
@@ -895,7 +933,7 @@ template <int R>
 __device__ __forceinline__ void decode_store_windowed(const MatDev& d, uint32_t pos, __nv_bfloat16* orow,
                                                       int col0, uint16_t* stage, int lane, uint64_t limit) {
     constexpr int kChunkK = (kWinWords - 8) / R;
-    static_assert(RB_LAYOUT == 1 && RB_ALIGNTAB, "windowed passes use the PTX symbol step");
+    static_assert(RB_LAYOUT == 1 && (RB_ALIGNTAB || RB_TABCOPIES == 2), "windowed passes use the PTX symbol step");
     const SmemMap sm = smem_map(0);
     const uint32_t magic = __shfl_sync(0xffffffffu, 0x4B000000u, 0);
     uint8_t* const wgen = reinterpret_cast<uint8_t*>(stage) + lane * kWinBytes;
@@ -917,7 +955,7 @@ __device__ __forceinline__ void decode_store_windowed(const MatDev& d, uint32_t 
             __nv_bfloat16* o = orow + 32 * k;
 #pragma unroll
             for (int r = 0; r < R; ++r)
-                o[roff[r]] = __float2bfloat16(sym_code(st, w, pw, sm.tab_s, sm.tab, true, d, magic) * sv);
+                o[roff[r]] = __float2bfloat16(sym_code(st, w, pw, tab_lane_base(sm.tab_s), sm.tab, true, d, magic) * sv);
         }
         p += (pw - pw0) >> 1;
     }
