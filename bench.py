@@ -215,8 +215,8 @@ def read_peak():
 
 
 def read_traffic(workload):
-    """dram bytes per launch of the chain kernel recorded by the committed ncu
-    summary for this workload, if any."""
+    """dram bytes per launch of the chain kernel over the config's full layer
+    count, recorded by the committed ncu summary for this workload, if any."""
     p = os.path.join(ROOT, "profiles", f"gemv_chain_kernel_{workload}.txt")
     if not os.path.exists(p):
         return None
@@ -630,6 +630,8 @@ def main():
     peak, peak_kind = read_peak()
     achieved = alg_bytes / (k_ms * 1e-3) / 1e9
     traffic = read_traffic(workload_name(args.config, args.R)) if world == 1 else None
+    if traffic is not None:
+        traffic *= nlayers / nl   # the summary's figure is for the config's full layer count
     compressed_total = alg_bytes
     if world > 1:
         t_b = torch.tensor([float(alg_bytes)], device=device, dtype=torch.float64)

@@ -1790,8 +1790,8 @@ namespace rb200 {
 // Memory ordering.  A CTA finishing a chunk: bar.sync, then one thread fences
 // (gpu scope; system scope when its rows were also stored to peer GPUs) and
 // increments the phase's completion counter.  The CTA that completes a phase
-// on a multi-GPU plan then adds 1 to that phase's arrival counter on every
-// rank (red.release.sys).  A waiting thread reads the counters with
+// on a multi-GPU plan then fences at system scope once more and adds 1 to
+// that phase's arrival counter on every rank (relaxed reductions).  A waiting thread reads the counters with
 // ld.acquire, then bar.sync, then reads activations with weak L1-cached loads.
 //
 // The last CTA to leave resets the queue and completion counters and counts
@@ -1800,6 +1800,7 @@ namespace rb200 {
 // status set: launches return at once until rans_gemv_chain_status has read
 // and cleared it (multi-GPU plans must then be planned again on every rank).
 constexpr int32_t kChainTimeout = 1;
+constexpr int kDoneStride = 32;   // one 128-byte line per phase's completion counter
 
 struct ChainHeader {
     int ndesc, nchunks, R, nphases;
@@ -1807,7 +1808,7 @@ struct ChainHeader {
     int shift;                 // kernel phase = caller phase + shift (1 when activations are prescaled up front)
     int pad0;
     int64_t phase_off;         // int32 phase_end[nphases]: chunks [phase_end[p-1], phase_end[p]) are phase p
-    int64_t ctl_off;           // ChainCtl, then uint32 done[nphases]
+    int64_t ctl_off;           // ChainCtl, then uint32 done[nphases * kDoneStride] (one line per phase)
     int64_t timeout_ns;        // bound of every dependency wait
     int64_t jobs_off;          // PrescaleJob[] of the activation prescale chunks
     uint32_t* arrive;          // this rank's arrival counters [nphases] (multi-GPU), or null
@@ -1833,8 +1834,8 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
     asm volatile("ld.acquire.sys.global.u32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
     return v;
 }
-__device__ __forceinline__ void red_release_sys(uint32_t* p, uint32_t v) {
-    asm volatile("red.release.sys.global.add.u32 [%0], %1;\n" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ void red_relaxed_sys(uint32_t* p, uint32_t v) {
+    asm volatile("red.relaxed.sys.global.add.u32 [%0], %1;\n" ::"l"(p), "r"(v) : "memory");
 }
 __device__ __forceinline__ uint64_t global_ns() {
     uint64_t t;
@@ -1874,7 +1875,7 @@ __device__ bool chain_wait(const ChainHeader* h, int p) {
     uint64_t t0 = 0;
     unsigned sleep_ns = 32;
     for (;;) {
-        const bool local = ld_acquire_gpu(done + p) >= need;
+        const bool local = ld_acquire_gpu(done + p * kDoneStride) >= need;
         const bool peers = h->npeer == 0 || (int32_t)(ld_acquire_sys(h->arrive + p) - need_arrive) >= 0;
         if (local && peers) return true;
         if (*reinterpret_cast<volatile int32_t*>(&ctl->status) != 0) return false;
@@ -1916,13 +1917,18 @@ __device__ __forceinline__ int chain_grab(const ChainHeader* h) {
 __device__ __forceinline__ void chain_signal(const ChainHeader* h, int p, uint32_t count) {
     uint32_t* done = reinterpret_cast<uint32_t*>(chain_ctl(h) + 1);
     if (h->npeer > 0) {
-        __threadfence_system();
-        const uint32_t prev = atomicAdd(done + p, count);
-        if (prev + count == phase_chunks(chain_phase_end(h), p))
-            for (int q = 0; q < h->npeer; ++q) red_release_sys(h->arrive_peer[q] + p, 1u);
+        __threadfence_system();   // this CTA's stores, peers' rows included, before its count
+        const uint32_t prev = atomicAdd(done + p * kDoneStride, count);
+        if (prev + count == phase_chunks(chain_phase_end(h), p)) {
+            // every CTA of this rank has published phase p: one system fence
+            // orders all of it before the signals, which then need no fence of
+            // their own (a release per peer would serialise one per rank)
+            __threadfence_system();
+            for (int q = 0; q < h->npeer; ++q) red_relaxed_sys(h->arrive_peer[q] + p, 1u);
+        }
     } else {
         __threadfence();
-        atomicAdd(done + p, count);
+        atomicAdd(done + p * kDoneStride, count);
     }
 }
 
@@ -2004,7 +2010,7 @@ __global__ void __launch_bounds__(kThreads, RB_MINB) gemv_chain_kernel(const Cha
         const uint32_t n = atomicAdd(&ctl->exited, 1u);
         if (n + 1 == gridDim.x) {
             uint32_t* done = reinterpret_cast<uint32_t*>(ctl + 1);
-            for (int p = 0; p < hdr->nphases; ++p) done[p] = 0u;
+            for (int p = 0; p < hdr->nphases; ++p) done[p * kDoneStride] = 0u;
             ctl->queue = 0u;
             ctl->exited = 0u;
             ctl->epoch = *reinterpret_cast<volatile uint32_t*>(&ctl->epoch) + 1u;
@@ -2171,7 +2177,7 @@ static int layout_chain(const RansGemvDesc* descs, const int* phase, int n, int 
     L.jobs_off = align16(sizeof(ChainHeader) + sizeof(MatDev) * L.mats.size() + sizeof(Chunk) * nch);
     L.phase_off = align16(L.jobs_off + sizeof(PrescaleJob) * L.jobs.size());
     L.ctl_off = align16(L.phase_off + sizeof(int) * (size_t)L.nphases);
-    L.counters_off = align16(L.ctl_off + sizeof(ChainCtl) + sizeof(uint32_t) * (size_t)L.nphases);
+    L.counters_off = align16(L.ctl_off + sizeof(ChainCtl) + sizeof(uint32_t) * kDoneStride * (size_t)L.nphases);
     L.partials_off = align16(L.counters_off + sizeof(uint32_t) * (size_t)ncounters);
     L.xprime_off = align16(L.partials_off + sizeof(float) * (size_t)npartials);
     L.bytes = L.xprime_off + xbytes;
