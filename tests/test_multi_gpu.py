@@ -41,3 +41,18 @@ def test_two_gpu_chain_exchange_checks(cuda_ok):
     assert line["n_gpus"] == 2
     assert line["check"]["ok"], line["check"]
     assert line["check"]["exchange_identical_on_all_ranks"]
+
+
+def test_two_gpu_chain_phases_feed_each_other(cuda_ok):
+    """Phase k reads the full output of phase k-1 exchanged inside the same
+    launch (tests/mgpu_chain_feed.py): every phase on every rank must match the
+    oracle over 20 launches whose outputs are reset to NaN first."""
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           "--nproc-per-node", "2", "--master-addr", "127.0.0.1", "--master-port", str(_port()),
+           os.path.join(ROOT, "tests", "mgpu_chain_feed.py")]
+    out = subprocess.run(cmd, capture_output=True, text=True, cwd=ROOT, timeout=400)
+    assert out.returncode == 0, out.stderr[-3000:]
+    assert "chain feed ok" in out.stdout

@@ -1991,9 +1991,11 @@ __global__ void __launch_bounds__(kThreads, RB_MINB) gemv_chain_kernel(const Cha
         if (threadIdx.x == 0) {
             pend_phase = phase;
             ++pend;
-            if (!(ch.phase & kChainAhead)) {
+            if (!(ch.phase & kChainAhead) && hdr->npeer == 0) {
                 // one of the phase's last chunks: its completion may be what
-                // the next phase waits for, publish it now
+                // the next phase waits for, publish it now (multi-GPU plans
+                // publish once per phase and CTA: each publication fences at
+                // system scope, an NVLink round trip that stalls warp 0)
                 chain_signal(hdr, phase, pend);
                 pend = 0;
             }

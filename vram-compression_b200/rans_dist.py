@@ -199,11 +199,16 @@ class ShardedChain:
     """This rank's share of a dependency-ordered decoder step (phases) whose
     projections are row-sharded over the ranks of the default process group.
 
-    mats / full_rows / xs as for ShardedStep; phases[i] is projection i's
-    phase.  One call is one kernel launch on this rank: phase p+1 starts once
+    mats / full_rows / xs as for ShardedStep, except that xs[i] may be an int
+    j: projection i then reads the FULL output of projection j (fp32, already
+    multiplied by the step: the pre-scaled convention), produced by an earlier
+    phase of the same launch and exchanged by the kernel; phases[i] is
+    projection i's phase.  One call is one kernel launch on this rank: phase p+1 starts once
     every rank has stored its rows of phase p into every rank's `y_full`
-    (symmetric memory) and signalled it.  After a call, `full[i]` is
-    projection i's complete output on this rank.  Every rank must call the
+    (symmetric memory) and signalled it.  `full[i]` is projection i's complete
+    output on this rank once every rank's launch has ended (nothing inside the
+    kernel waits for the last phase: synchronise and pass a barrier before
+    reading it on the host).  Every rank must call the
     same number of times; check() synchronises and raises
     rans_b200.ChainTimeout if a wait ran out (then build the chain again on
     every rank).
@@ -236,13 +241,17 @@ class ShardedChain:
         arrive_peer = [int(p) for p in self.hdl_arrive.buffer_ptrs]
         sl = self.layout.local_slices(self.rank)
         ys = [self.y_full[a:b] for a, b in sl]
+        self.full = [self.y_full[int(self.layout.F[i]):int(self.layout.F[i]) + self.layout.rows[i]]
+                     for i in range(len(mats))]
+        feeds = [isinstance(x, int) for x in xs]
+        xs = [self.full[x] if f else x for x, f in zip(xs, feeds)]
+        pre = list(prescaled_x) if isinstance(prescaled_x, (list, tuple)) else [bool(prescaled_x)] * len(mats)
+        pre = [p or f for p, f in zip(pre, feeds)]
         torch.cuda.synchronize()
-        self.chain = rb.RansChain(mats, xs, ys, phases, lib=lib, prescaled_x=prescaled_x, timeout_ms=timeout_ms,
+        self.chain = rb.RansChain(mats, xs, ys, phases, lib=lib, prescaled_x=pre, timeout_ms=timeout_ms,
                                   sync=(self.world, self.rank, self.arrive.data_ptr(), arrive_peer, peers))
         # every rank has zeroed its arrival counters before any rank launches
         dist.barrier()
-        self.full = [self.y_full[int(self.layout.F[i]):int(self.layout.F[i]) + self.layout.rows[i]]
-                     for i in range(len(mats))]
         self.kernels = 1
 
     def __call__(self):
