@@ -132,14 +132,16 @@ int rans_gemv_step_kernels(const void* workspace);
  * {gate,up} -> down: phase p+1 reads what phase p wrote), run from ONE
  * persistent grid.  phase[i] (0..P-1, every phase non-empty) is descriptor
  * i's phase; chunks of phase p start only after every chunk of phase p-1 has
- * finished (and, with `sync`, after every rank has signalled phase p-1).  The
- * table load and an L2 warm-up of the weights of a waiting chunk overlap the
- * previous phase.  Activations are read with coherent loads after the wait,
+ * finished (and, with `sync`, after every rank has signalled phase p-1).
+ * Weights are independent of the previous phase: the table load and each
+ * warp's staging of its words overlap it; a warp waits right before its first
+ * activation load.  Activations are read with coherent loads after the wait,
  * so phase p+1's x may be phase p's y (the fp32 pre-scaled convention: step
  * NULL).  A bf16 x (step given) must be written before the launch: the kernel
- * turns it into fp32 x*step in the workspace one phase ahead of its use.  No counterpart in the reference, whose harness
- * launches one kernel per matrix (kernel/bench.py:104-107,
- * kernel/rans.py:147-151); this is the layer-level launcher of its survey.   */
+ * turns it into fp32 x*step in the workspace one phase ahead of its use.  No
+ * counterpart in the reference, whose harness launches one kernel per matrix
+ * (kernel/bench.py:104-107, kernel/rans.py:147-151); this is the layer-level
+ * launcher of its survey. */
 
 /* Row-sharded chain over the GPUs of one node (one process per GPU).
  * arrive: this rank's uint32[P+1] arrival counters (the chain may add one
@@ -152,7 +154,9 @@ int rans_gemv_step_kernels(const void* workspace);
  * the phase is complete on a rank once all ranks have added 1 to its counter
  * there.  A faster rank may already run the next launch's first phase while
  * a slower one runs this launch's last, so phase 0's outputs must not be
- * read by the last phase. */
+ * read by the last phase; and nothing waits for the last phase inside the
+ * kernel, so its rows from other ranks are complete on this rank only once
+ * every rank's launch has ended (synchronise and pass a host barrier). */
 typedef struct RansChainSync {
     int32_t nranks;                  /* <= 8 */
     int32_t rank;
