@@ -1102,7 +1102,7 @@ static int64_t pass_symbols(const MatDev& d) {
 // Fills the work decomposition of d.  `split_for` > 0 is the number of warps
 // resident at once and allows column blocks to be split across warps
 // (accumulating into y) where that shortens the launch.
-static void plan_matrix(MatDev& d, int R, int split_for) {
+static void plan_matrix(MatDev& d, int R, int split_for, int kcap = 4) {
     d.ncb = d.cols / d.C;
     d.nrb = d.rows / R;
     d.nk = d.C / 32;
@@ -1116,7 +1116,7 @@ static void plan_matrix(MatDev& d, int R, int split_for) {
     // K that divides ncb (no idle stream slots), preferring more streams per
     // lane, with at most pass_symbols(d) symbols per pass so that the pass's
     // words fit the stage.
-    const int kmax = (int)std::max<int64_t>(1, std::min<int64_t>(4, pass_symbols(d) / ((int64_t)R * d.C)));
+    const int kmax = (int)std::max<int64_t>(1, std::min<int64_t>(kcap, pass_symbols(d) / ((int64_t)R * d.C)));
     int k = 1;
     for (int c = kmax; c >= 2; --c)
         if (d.ncb % c == 0) { k = c; break; }
@@ -1400,13 +1400,13 @@ static size_t step_bytes(int ndesc, int64_t nchunks) {
     return sizeof(StepHeader) + sizeof(MatDev) * (size_t)ndesc + sizeof(Chunk) * (size_t)nchunks;
 }
 
-static int64_t count_chunks(const RansGemvDesc* descs, int n, int R, std::vector<MatDev>* out) {
+static int64_t count_chunks(const RansGemvDesc* descs, int n, int R, std::vector<MatDev>* out, int kcap = 4) {
     int64_t nchunks = 0;
     for (int i = 0; i < n; ++i) {
         const RansGemvDesc& s = descs[i];
         if (!shape_ok(R, s.rows, s.cols, s.C)) return -1;
         MatDev d = make_desc(s.words, s.offs, s.table, s.x, s.step, s.y, s.rows, s.cols, s.C, s.nwords);
-        plan_matrix(d, R, 0);
+        plan_matrix(d, R, 0, kcap);
         nchunks += (d.nitems + kWarps - 1) / kWarps;
         if (out) out->push_back(d);
     }
@@ -1438,7 +1438,7 @@ static int chunk_items(const MatDev& d) { return d.combine ? (kWarps / d.nseg) *
 // latency-bound groups are split into segments, groups of a few waves cut
 // into row segments.  Adds the segment counters and partials the group needs;
 // returns true when the group was planned as latency-bound (split).
-static bool plan_group(std::vector<MatDev>& mats, int R, int64_t& ncounters, int64_t& npartials) {
+static bool plan_group(std::vector<MatDev>& mats, int R, int64_t& ncounters, int64_t& npartials, int kcap = 4) {
     int64_t items = 0;
     for (const MatDev& d : mats) items += d.nitems;
     const bool split = items * 2 < split_target();
@@ -1459,7 +1459,7 @@ static bool plan_group(std::vector<MatDev>& mats, int R, int64_t& ncounters, int
         }
         auto next_t = [&](size_t i) {
             const MatDev& d = mats[i];
-            for (int t = T[i] + 1; t <= 4 && (int64_t)t * R * d.C <= pass_symbols(d); ++t)
+            for (int t = T[i] + 1; t <= kcap && (int64_t)t * R * d.C <= pass_symbols(d); ++t)
                 if (d.ncb % t == 0) return t;
             return 0;
         };
@@ -1504,7 +1504,7 @@ static bool plan_group(std::vector<MatDev>& mats, int R, int64_t& ncounters, int
             if (d.ncb <= d.kcol) continue;
             const int share = (int)std::max<int64_t>(1, W * d.nitems / items);
             MatDev sp = d;
-            plan_matrix(sp, R, share);
+            plan_matrix(sp, R, share, kcap);
             if (sp.nseg <= 1 || sp.kcol != d.kcol) continue;
             d = sp;
             d.accumulate = 0;
@@ -2037,6 +2037,15 @@ struct ChainLayout {
 };
 
 constexpr int kPrescaleCols = 8192;    // columns per activation prescale chunk
+// Most tiles one chain item decodes at once (the launch planner's limit, 4).
+// Smaller items give a phase more CTA chunks to balance, but measured slower
+// on B200: 8 layers of the 70B-shaped chain 4.92 ms at 4 tiles, 5.39 at 2,
+// 6.75 at 1; one rank's eighth of the 80-layer step 9.49 / 10.36 / 11.90 ms
+// (each item's staging, reduction and epilogue cost more than balance gains).
+#ifndef RB_CHAIN_TILES
+#define RB_CHAIN_TILES 4
+#endif
+constexpr int kChainTiles = RB_CHAIN_TILES;
 
 // The chain's work list.  Caller phase p becomes kernel phase p + shift; a
 // matrix with bf16 activations (written before the launch) reads a prescaled
@@ -2055,7 +2064,7 @@ static int layout_chain(const RansGemvDesc* descs, const int* phase, int n, int 
     for (int p = 0; p < P; ++p)
         if (members[p].empty()) return -2;   // phases are numbered 0..P-1 without gaps
     L.mats.clear();
-    if (count_chunks(descs, n, R, &L.mats) < 0) return -2;
+    if (count_chunks(descs, n, R, &L.mats, kChainTiles) < 0) return -2;
     int64_t ncounters = 0, npartials = 0;
     L.parent.resize(n);
     for (int i = 0; i < n; ++i) L.parent[i] = i;
@@ -2066,7 +2075,7 @@ static int layout_chain(const RansGemvDesc* descs, const int* phase, int n, int 
         // each phase runs on the whole GPU by itself: plan it like one launch
         std::vector<MatDev> g;
         for (int i : members[p]) g.push_back(L.mats[i]);
-        plan_group(g, R, ncounters, npartials);
+        plan_group(g, R, ncounters, npartials, kChainTiles);
         int64_t items = 0;
         for (size_t k = 0; k < g.size(); ++k) {
             L.mats[members[p][k]] = g[k];
