@@ -578,6 +578,9 @@ def main():
         diff = max(float((u - v).norm() / v.norm().clamp_min(1e-30)) for u, v in zip(outputs, ys_p))
         compare = {"independent_batch": {"us_per_step": round(batch_ms * 1e3, 1),
                                          "gbs": round(2.0 * weights_full / (batch_ms * 1e-3) / 1e9, 1),
+                                         "compressed_gbs": round(algorithmic_bytes(meta) / (batch_ms * 1e-3) / 1e9, 1),
+                                         "roofline_frac": round(algorithmic_bytes(meta) / (batch_ms * 1e-3) / 1e9
+                                                                / read_peak()[0], 4),
                                          "how": "all projections as one independent batch "
                                                 "(rans_gemv_step_launch; ignores the phase order)"},
                    "per_phase_graph": {"us_per_step": round(graph_ms * 1e3, 1),

@@ -141,3 +141,31 @@ def test_chain_wait_that_never_ends_reports_and_recovers(torch, rb):
     y = m.gemv_bf16(x)
     torch.cuda.synchronize()
     _check_y(y.cpu().numpy(), orc.gemv(codes, step.astype(np.float64), x.float().cpu().numpy().astype(np.float64)))
+
+
+@pytest.mark.parametrize("R", [1, 2, 4, 16])
+def test_chain_every_tile_height(torch, rb, R):
+    """The chain launcher at every R the format allows: two latency-bound
+    phases and a multi-wave one, the last feeding on the second's output."""
+    rng = np.random.default_rng(40 + R)
+    shapes = [(256, 1024), (512, 1024), (256 * 40, 512)]   # third: x = phase-1 output (512 rows)
+    mats, codes_l, steps = [], [], []
+    for i, (rows, cols) in enumerate(shapes):
+        c = orc.synth_codes(rows, cols, 3.25, "laplace", seed=70 + 3 * R + i)
+        step = (0.01 * rng.uniform(0.5, 1.5, cols)).astype(np.float32) if i < 2 else np.ones(cols, np.float32)
+        mats.append(rb.RansMatrix(rb.encode(c, R, 512), torch.from_numpy(step)))
+        codes_l.append(c)
+        steps.append(step)
+    x0 = torch.from_numpy(rng.standard_normal(1024).astype(np.float32)).bfloat16().cuda()
+    ys = [torch.full((r,), float("nan"), device="cuda") for r, _ in shapes]
+    ch = rb.RansChain(mats, [x0, x0, ys[1]], ys, [0, 1, 2], prescaled_x=[False, False, True])
+    for _ in range(3):
+        for y in ys:
+            y.fill_(float("nan"))
+        ch()
+    ch.check()
+    torch.cuda.synchronize()
+    xb = x0.float().cpu().numpy().astype(np.float64)
+    for k in range(2):
+        _check_y(ys[k].cpu().numpy(), orc.gemv(codes_l[k], steps[k].astype(np.float64), xb))
+    _check_y(ys[2].cpu().numpy(), orc.gemv(codes_l[2], np.ones(512), ys[1].cpu().numpy().astype(np.float64)))
