@@ -180,11 +180,21 @@ __device__ __forceinline__ uint32_t relayout_entry(uint32_t e) {
 #endif
 }
 
+// Every kernel that calls this runs kThreads threads: a compile-time stride
+// lets each thread issue all of its loads before the first store (one L2
+// round trip per table instead of one per few entries).
 __device__ __forceinline__ void load_table(uint32_t* tab, const uint32_t* __restrict__ table) {
-    for (int i = threadIdx.x; i < (int)kProbM; i += blockDim.x) {
-        const uint32_t e = relayout_entry(__ldg(table + i));
+    static_assert(kProbM % kThreads == 0, "table entries per thread");
+    constexpr int kPer = kProbM / kThreads;
+    uint32_t e[kPer];
 #pragma unroll
-        for (int c = 0; c < kTabCopies; ++c) tab[i * kTabCopies + c] = e;
+    for (int k = 0; k < kPer; ++k) e[k] = __ldg(table + threadIdx.x + k * kThreads);
+#pragma unroll
+    for (int k = 0; k < kPer; ++k) {
+        const uint32_t v = relayout_entry(e[k]);
+        const int i = threadIdx.x + k * kThreads;
+#pragma unroll
+        for (int c = 0; c < kTabCopies; ++c) tab[i * kTabCopies + c] = v;
     }
 }
 
@@ -1898,12 +1908,19 @@ __device__ bool chain_wait(const ChainHeader* h, int p) {
 constexpr int kChainAhead = 1 << 30;
 constexpr int kChainPhaseMask = kChainAhead - 1;
 
-// Thread 0: the next chunk of the queue (nchunks once it is empty or an
-// error was reported).
+// Thread 0: a chunk taken from the queue (`raw`, the queue's old value) as
+// the index to run -- nchunks once the queue is empty or an error was
+// reported (`status`, read no earlier than the atomic was issued).
+__device__ __forceinline__ int chain_take(const ChainHeader* h, uint32_t raw, int32_t status) {
+    return status != 0 ? h->nchunks : (int)min(raw, (uint32_t)h->nchunks);
+}
+
+// Thread 0: the next chunk of the queue.  The atomic and the status read are
+// issued together (one round trip, not two).
 __device__ __forceinline__ int chain_grab(const ChainHeader* h) {
     ChainCtl* ctl = chain_ctl(h);
-    if (*reinterpret_cast<volatile int32_t*>(&ctl->status) != 0) return h->nchunks;
-    return (int)min(atomicAdd(&ctl->queue, 1u), (uint32_t)h->nchunks);
+    const uint32_t raw = atomicAdd(&ctl->queue, 1u);
+    return chain_take(h, raw, *reinterpret_cast<volatile int32_t*>(&ctl->status));
 }
 
 // Thread 0: publish `count` finished chunks of phase p -- every output they
@@ -1938,7 +1955,13 @@ __global__ void __launch_bounds__(kThreads, RB_MINB) gemv_chain_kernel(const Cha
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const SmemMap sm = smem_map(warp);
     const uint32_t* cur = nullptr;    // table now in shared memory
-    int next = -1;                    // thread 0: chunk taken ahead, or -1
+    // thread 0: a chunk taken ahead -- the queue's old value and the status,
+    // both read when this chunk starts and first used when it ends, so the
+    // round trip overlaps the chunk instead of delaying its start
+    bool ahead = false;
+    uint32_t ahead_raw = 0;
+    int32_t ahead_status = 0;
+    int cur_desc = -1;                // descriptor whose table `cur` is
     int pend_phase = -1;              // thread 0: phase of finished, unpublished chunks
     uint32_t pend = 0;                //           and how many
     if (threadIdx.x == 0) {
@@ -1957,7 +1980,12 @@ __global__ void __launch_bounds__(kThreads, RB_MINB) gemv_chain_kernel(const Cha
                 chain_signal(hdr, pend_phase, pend);   // before any wait of this chunk
                 pend = 0;
             }
-            if (ch.phase & kChainAhead) next = chain_grab(hdr);   // used at the end of this chunk
+            if (ch.phase & kChainAhead) {
+                ChainCtl* ctl = chain_ctl(hdr);
+                ahead_raw = atomicAdd(&ctl->queue, 1u);
+                ahead_status = *reinterpret_cast<volatile int32_t*>(&ctl->status);
+                ahead = true;
+            }
         }
         if (ch.nitems < 0) {
             // activation prescale job: x' = bf16 x * step for columns
@@ -1972,9 +2000,12 @@ __global__ void __launch_bounds__(kThreads, RB_MINB) gemv_chain_kernel(const Cha
             // weights are immutable: the table load and each warp's staging
             // and state reads overlap the previous phase; each warp waits for
             // it only before its first activation load (dep_wait)
-            if (d.table != cur) {
-                load_table(sm.tab, d.table);
-                cur = d.table;
+            if (ch.desc != cur_desc) {    // a descriptor's table pointer is read once per change
+                if (d.table != cur) {
+                    load_table(sm.tab, d.table);
+                    cur = d.table;
+                }
+                cur_desc = ch.desc;
             }
             if (threadIdx.x == 0) g_chain_wait = phase > 0 ? phase - 1 : -1;
             __syncthreads();
@@ -1988,21 +2019,26 @@ __global__ void __launch_bounds__(kThreads, RB_MINB) gemv_chain_kernel(const Cha
             }
         }
         __syncthreads();   // every output of chunk c is written
+        bool publish = false;
         if (threadIdx.x == 0) {
             pend_phase = phase;
             ++pend;
-            if (!(ch.phase & kChainAhead) && hdr->npeer == 0) {
-                // one of the phase's last chunks: its completion may be what
-                // the next phase waits for, publish it now (multi-GPU plans
-                // publish once per phase and CTA: each publication fences at
-                // system scope, an NVLink round trip that stalls warp 0)
-                chain_signal(hdr, phase, pend);
-                pend = 0;
-            }
-            s_chunk = next >= 0 ? next : chain_grab(hdr);
-            next = -1;
+            // one of the phase's last chunks: its completion may be what the
+            // next phase waits for, publish it now (multi-GPU plans publish
+            // once per phase and CTA: each publication fences at system
+            // scope, an NVLink round trip that stalls warp 0)
+            publish = !(ch.phase & kChainAhead) && hdr->npeer == 0;
+            s_chunk = ahead ? chain_take(hdr, ahead_raw, ahead_status) : chain_grab(hdr);
+            ahead = false;
         }
         __syncthreads();
+        if (publish) {
+            // after the barrier, so the other warps start the next chunk
+            // meanwhile; thread 0 observed every output of chunk c at the
+            // barrier above, so its fence still orders them before the count
+            chain_signal(hdr, phase, pend);
+            pend = 0;
+        }
     }
     if (threadIdx.x == 0) {
         if (pend > 0) chain_signal(hdr, pend_phase, pend);
