@@ -2019,26 +2019,28 @@ __global__ void __launch_bounds__(kThreads, RB_MINB) gemv_chain_kernel(const Cha
             }
         }
         __syncthreads();   // every output of chunk c is written
-        bool publish = false;
         if (threadIdx.x == 0) {
             pend_phase = phase;
             ++pend;
-            // one of the phase's last chunks: its completion may be what the
-            // next phase waits for, publish it now (multi-GPU plans publish
-            // once per phase and CTA: each publication fences at system
-            // scope, an NVLink round trip that stalls warp 0)
-            publish = !(ch.phase & kChainAhead) && hdr->npeer == 0;
-            s_chunk = ahead ? chain_take(hdr, ahead_raw, ahead_status) : chain_grab(hdr);
+            // the next chunk: taken ahead, or the queue atomic issued now,
+            // before the publication below, so the two round trips overlap
+            if (!ahead) {
+                ChainCtl* ctl = chain_ctl(hdr);
+                ahead_raw = atomicAdd(&ctl->queue, 1u);
+                ahead_status = *reinterpret_cast<volatile int32_t*>(&ctl->status);
+            }
+            if (!(ch.phase & kChainAhead) && hdr->npeer == 0) {
+                // one of the phase's last chunks: its completion may be what
+                // the next phase waits for, publish it now (multi-GPU plans
+                // publish once per phase and CTA: each publication fences at
+                // system scope, an NVLink round trip that stalls warp 0)
+                chain_signal(hdr, phase, pend);
+                pend = 0;
+            }
+            s_chunk = chain_take(hdr, ahead_raw, ahead_status);
             ahead = false;
         }
         __syncthreads();
-        if (publish) {
-            // after the barrier, so the other warps start the next chunk
-            // meanwhile; thread 0 observed every output of chunk c at the
-            // barrier above, so its fence still orders them before the count
-            chain_signal(hdr, phase, pend);
-            pend = 0;
-        }
     }
     if (threadIdx.x == 0) {
         if (pend > 0) chain_signal(hdr, pend_phase, pend);
