@@ -58,6 +58,9 @@ constexpr int kPadWords = 8;
 #ifndef RB_PDL
 #define RB_PDL 1         // programmatic dependent launch of the step kernel
 #endif
+#ifndef RB_POLL_MAX_NS
+#define RB_POLL_MAX_NS 256   // chain waits: longest sleep between two polls of a completion counter
+#endif
 #ifndef RB_PREFETCH
 #define RB_PREFETCH 0    // each CTA warms L2 for the chunk one wave ahead (measured: no gain)
 #endif
@@ -1897,7 +1900,7 @@ __device__ bool chain_wait(const ChainHeader* h, int p) {
             return false;
         }
         __nanosleep(sleep_ns);
-        if (sleep_ns < 256) sleep_ns *= 2;
+        if (sleep_ns < RB_POLL_MAX_NS) sleep_ns *= 2;
     }
 }
 
