@@ -168,6 +168,20 @@ typedef struct RansChainSync {
 /* Device workspace bytes for this chain; -1 bad R, -2 bad shape or phases. */
 int64_t rans_gemv_chain_workspace_bytes(const RansGemvDesc* descs, const int* phase, int n, int R);
 
+/* The chain's work list as the planner hands it out, without a GPU (no
+ * counterpart in the reference: plan introspection for tests and tuning).
+ * Writes up to max_chunks records of 8 int32 to `out` (may be NULL), in
+ * hand-out order: kernel phase (the caller's phase, plus 1 when an activation
+ * prescale phase runs in front); the caller's matrix index; kind (0 decode,
+ * 1 activation prescale); then for decode the first item, the item count
+ * (at most one per warp of a CTA), tiles per item, streams interleaved per
+ * lane and segments per row block (item i covers row block i / segments,
+ * tiles [(i % segments) * tiles, ... + tiles) clipped to the matrix), and for
+ * prescale the first column and the column count.  Returns the number of
+ * chunks, -1 bad R, -2 bad shape or phases. */
+int64_t rans_gemv_chain_describe(const RansGemvDesc* descs, const int* phase, int n, int R,
+                                 int32_t* out, int64_t max_chunks);
+
 /* Plan the chain into `workspace` (HOST arrays descs, phase; sync NULL on one
  * GPU).  timeout_ms bounds every dependency wait of the kernel.  Returns the
  * launch grid (the CTAs resident at once, at most the number of chunks) in

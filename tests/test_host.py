@@ -171,6 +171,70 @@ def test_step_workspace_layout_without_gpu(lib):
     assert lib.rans_gemv_step_workspace_bytes(_descs(1, 256, 1536, 512, True), 1, 3) == -1  # bad R
 
 
+def _chain_describe(lib, shapes, phases, R, steps):
+    """Chunk records of the chain planner for `shapes` [(rows, cols, C)]."""
+    import ctypes
+    n = len(shapes)
+    arr = (rb.RansGemvDesc * n)()
+    for i, (rows, cols, C) in enumerate(shapes):
+        nwords = int(rows * cols * 2.6 / 16) + 8                 # ~2.25 b/w payload + stream overhead
+        arr[i] = rb.RansGemvDesc(256, 256, 256, 256, 256 if steps[i] else None, 256, nwords, rows, cols, C, 0)
+    ph = (ctypes.c_int * n)(*phases)
+    nc = lib.rans_gemv_chain_describe(ctypes.addressof(arr), ctypes.addressof(ph), n, R, None, 0)
+    assert nc > 0, nc
+    out = (ctypes.c_int32 * (8 * nc))()
+    assert lib.rans_gemv_chain_describe(ctypes.addressof(arr), ctypes.addressof(ph), n, R, out, nc) == nc
+    return np.frombuffer(out, dtype=np.int32).reshape(nc, 8).copy()
+
+
+@pytest.mark.parametrize("case", ["llama70b", "llama70b_rank_of_2", "llama70b_rank_of_8", "qwen_R16", "qwen_R1_fp32"])
+def test_chain_plan_covers_every_tile_once_without_gpu(lib, case):
+    """The chain planner's work list (rans_gemv_chain_describe, no GPU): every
+    tile of every matrix is decoded by exactly one item, whatever mix of whole
+    items, latency splits and half-size tail items the planner chose; phases
+    are handed out in order, each matrix in its own phase (plus one when an
+    activation prescale phase runs in front); a chunk holds at most one item
+    per warp; and every bf16-activation matrix gets its columns prescaled
+    exactly once, one phase before its own."""
+    h, kv, f = 8192, 1024, 28672
+    llama = [(h, h, 512), (kv, h, 512), (kv, h, 512), (h, h, 512), (f, h, 512), (f, h, 512), (h, f, 512)]
+    qwen = [(1536, 1536, 512), (256, 1536, 512), (256, 1536, 512), (1536, 1536, 512),
+            (8960, 1536, 512), (8960, 1536, 512), (1536, 8960, 640)]
+    phase_of = [0, 0, 0, 1, 2, 2, 3]
+    layer, R, world, layers, bf16 = {
+        "llama70b": (llama, 8, 1, 2, True), "llama70b_rank_of_2": (llama, 8, 2, 2, True),
+        "llama70b_rank_of_8": (llama, 8, 8, 2, True), "qwen_R16": (qwen, 16, 1, 3, True),
+        "qwen_R1_fp32": (qwen, 1, 1, 2, False)}[case]
+    shapes = [(rows // world, cols, C) for _ in range(layers) for rows, cols, C in layer]
+    phases = [4 * l + p for l in range(layers) for p in phase_of]
+    steps = [bf16 and (i % 2 == 0 or p > 0) for i, p in enumerate(phases)]   # mixed bf16 / fp32 x
+    rec = _chain_describe(lib, shapes, phases, R, steps)
+    kphase, mat, kind, first, count, tiles, streams, nseg = rec.T
+    assert (np.diff(kphase) >= 0).all()                                   # phases in order
+    shift = 1 if any(s for s, p in zip(steps, phases) if p == 0) else 0
+    dec = kind == 0
+    assert (kphase[dec] == np.array(phases)[mat[dec]] + shift).all()
+    assert ((count[dec] >= 1) & (count[dec] <= 8)).all()
+    assert ((streams[dec] >= 1) & (streams[dec] <= 4) & (streams[dec] <= tiles[dec])).all()
+    for i, (rows, cols, C) in enumerate(shapes):
+        nrb, ncb = rows // R, cols // C
+        cov = np.zeros((nrb, ncb), dtype=np.int32)
+        for c in np.nonzero(dec & (mat == i))[0]:
+            for it in range(first[c], first[c] + count[c]):
+                rbk, seg = divmod(it, nseg[c])
+                cov[rbk, seg * tiles[c]:min(ncb, (seg + 1) * tiles[c])] += 1
+        assert (cov == 1).all(), f"matrix {i}: tiles decoded {cov.min()}..{cov.max()} times"
+        pre = np.nonzero((kind == 1) & (mat == i))[0]
+        if not steps[i]:
+            assert len(pre) == 0
+            continue
+        colcov = np.zeros(cols, dtype=np.int32)
+        for c in pre:
+            assert kphase[c] == phases[i] + shift - 1
+            colcov[first[c]:first[c] + count[c]] += 1
+        assert (colcov == 1).all()
+
+
 def test_chain_workspace_layout_without_gpu(lib):
     """Host-side chain planning: phases must be numbered 0..P-1 without gaps;
     the workspace holds the descriptors, the chunks of every phase, the phase

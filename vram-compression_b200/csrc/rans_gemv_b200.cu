@@ -2243,6 +2243,36 @@ extern "C" int64_t rans_gemv_chain_workspace_bytes(const RansGemvDesc* descs, co
     return (int64_t)L.bytes;
 }
 
+extern "C" int64_t rans_gemv_chain_describe(const RansGemvDesc* descs, const int* phase, int n, int R,
+                                            int32_t* out, int64_t max_chunks) {
+    if (!valid_R(R)) return -1;
+    ChainLayout L;
+    if (layout_chain(descs, phase, n, R, L) != 0) return -2;
+    const int64_t nc = (int64_t)L.chunks.size();
+    for (int64_t c = 0; out != nullptr && c < nc && c < max_chunks; ++c) {
+        const Chunk& ch = L.chunks[c];
+        int32_t* o = out + 8 * c;
+        o[0] = ch.phase;
+        if (ch.nitems < 0) {               // activation prescale: columns [item0, item0 - nitems)
+            o[1] = L.job_mat[ch.desc];
+            o[2] = 1;
+            o[3] = ch.item0;
+            o[4] = -ch.nitems;
+            o[5] = o[6] = o[7] = 0;
+        } else {
+            const MatDev& d = L.mats[ch.desc];
+            o[1] = L.parent[ch.desc];
+            o[2] = 0;
+            o[3] = ch.item0;
+            o[4] = ch.nitems;
+            o[5] = d.cbs;
+            o[6] = d.kcol;
+            o[7] = d.nseg;
+        }
+    }
+    return nc;
+}
+
 template <int R>
 static int chain_grid_t(int64_t nchunks) {
     static unsigned long long done = 0;

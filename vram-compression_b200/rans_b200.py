@@ -84,6 +84,8 @@ def _bind(lib):
     lib.rans_escape_decode.restype = _i32
     lib.rans_gemv_chain_workspace_bytes.argtypes = [_vp, _vp, _i32, _i32]
     lib.rans_gemv_chain_workspace_bytes.restype = _i64
+    lib.rans_gemv_chain_describe.argtypes = [_vp, _vp, _i32, _i32, _vp, _i64]
+    lib.rans_gemv_chain_describe.restype = _i64
     lib.rans_gemv_chain_plan.argtypes = [_vp, _vp, _i32, _i32, _vp, _i32, _vp, _sz, _vp, _vp]
     lib.rans_gemv_chain_plan.restype = _i32
     lib.rans_gemv_chain_launch.argtypes = [_i32, _vp, _i32, _vp]
