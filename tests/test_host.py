@@ -9,6 +9,7 @@ import hashlib
 
 import numpy as np
 import pytest
+from hypothesis import given, settings, strategies as st
 
 from conftest import GOLDEN, ROOT, golden_cases, load_case
 import rans_b200 as rb
@@ -171,13 +172,14 @@ def test_step_workspace_layout_without_gpu(lib):
     assert lib.rans_gemv_step_workspace_bytes(_descs(1, 256, 1536, 512, True), 1, 3) == -1  # bad R
 
 
-def _chain_describe(lib, shapes, phases, R, steps):
+def _chain_describe(lib, shapes, phases, R, steps, nbits=None):
     """Chunk records of the chain planner for `shapes` [(rows, cols, C)]."""
     import ctypes
     n = len(shapes)
     arr = (rb.RansGemvDesc * n)()
     for i, (rows, cols, C) in enumerate(shapes):
-        nwords = int(rows * cols * 2.6 / 16) + 8                 # ~2.25 b/w payload + stream overhead
+        bits = 2.6 if nbits is None else nbits[i]               # default ~2.25 b/w payload + overhead
+        nwords = int(rows * cols * bits / 16) + 8
         arr[i] = rb.RansGemvDesc(256, 256, 256, 256, 256 if steps[i] else None, 256, nwords, rows, cols, C, 0)
     ph = (ctypes.c_int * n)(*phases)
     nc = lib.rans_gemv_chain_describe(ctypes.addressof(arr), ctypes.addressof(ph), n, R, None, 0)
@@ -208,7 +210,10 @@ def test_chain_plan_covers_every_tile_once_without_gpu(lib, case):
     shapes = [(rows // world, cols, C) for _ in range(layers) for rows, cols, C in layer]
     phases = [4 * l + p for l in range(layers) for p in phase_of]
     steps = [bf16 and (i % 2 == 0 or p > 0) for i, p in enumerate(phases)]   # mixed bf16 / fp32 x
-    rec = _chain_describe(lib, shapes, phases, R, steps)
+    _check_chain_plan(_chain_describe(lib, shapes, phases, R, steps), shapes, phases, R, steps)
+
+
+def _check_chain_plan(rec, shapes, phases, R, steps):
     kphase, mat, kind, first, count, tiles, streams, nseg = rec.T
     assert (np.diff(kphase) >= 0).all()                                   # phases in order
     shift = 1 if any(s for s, p in zip(steps, phases) if p == 0) else 0
@@ -233,6 +238,28 @@ def test_chain_plan_covers_every_tile_once_without_gpu(lib, case):
             assert kphase[c] == phases[i] + shift - 1
             colcov[first[c]:first[c] + count[c]] += 1
         assert (colcov == 1).all()
+
+
+@settings(max_examples=60, deadline=None)
+@given(data=st.data())
+def test_chain_plan_random_shapes_without_gpu(lib, data):
+    """The same invariants on random chains: tile heights R 1-16, tile widths C
+    32-768, one to twenty column tiles, matrices of one row block up to
+    hundreds, 0.5-8 bits per weight (the stage holds fewer or more tiles per
+    pass), phases of any size, bf16 and fp32 activations mixed."""
+    R = data.draw(st.sampled_from([1, 2, 4, 8, 16]))
+    n = data.draw(st.integers(1, 9))
+    shapes, nbits = [], []
+    for _ in range(n):
+        C = 32 * data.draw(st.integers(1, 24))
+        shapes.append((R * data.draw(st.integers(1, 300)), C * data.draw(st.integers(1, 20)), C))
+        nbits.append(data.draw(st.floats(0.5, 8.0)))
+    raw = [data.draw(st.integers(0, n - 1)) for _ in range(n)]
+    used = sorted(set(raw))
+    phases = [used.index(v) for v in raw]                 # numbered 0..P-1 without gaps
+    steps = [data.draw(st.booleans()) for _ in range(n)]
+    rec = _chain_describe(lib, shapes, phases, R, steps, nbits)
+    _check_chain_plan(rec, shapes, phases, R, steps)
 
 
 def test_chain_workspace_layout_without_gpu(lib):
