@@ -129,6 +129,38 @@ def test_large_against_c_oracle(torch, rb, shape, R, C, dist, bits):
     assert torch.equal(dec, want)
 
 
+@pytest.mark.parametrize("kind", ["two", "extremes", "dominant"])
+@pytest.mark.parametrize("R", [1, 8, 16])
+def test_edge_distributions(torch, rb, kind, R):
+    """Code distributions at the edges of the 12-bit table: two symbols only
+    (one of them rare: long runs without a renormalisation word), the
+    alphabet's extremes -128 and 127 only, and one dominant symbol with up to
+    300 singletons (frequency 1 each).  Decode bit-exact against
+    bf16(code * step); both GEMV entry points against float64."""
+    rng = np.random.default_rng({"two": 1, "extremes": 2, "dominant": 3}[kind] * 100 + R)
+    rows, cols, C = 16 * R, 1536, 512
+    if kind == "two":
+        codes = np.where(rng.random((rows, cols)) < 0.002, 5, -3)
+    elif kind == "extremes":
+        codes = np.where(rng.random((rows, cols)) < 0.5, -128, 127)
+    else:
+        codes = np.zeros((rows, cols), np.int64)
+        idx = rng.choice(rows * cols, 300, replace=False)
+        codes.flat[idx] = rng.choice(np.r_[-128:0, 1:128], 300)
+    codes = codes.astype(np.int32)
+    step = (0.01 * rng.uniform(0.5, 1.5, cols)).astype(np.float32)
+    x = rng.standard_normal(cols).astype(np.float32)
+    enc = rb.encode(codes, R, C)
+    ref = orc.encode(codes, R, C)
+    assert np.array_equal(enc["words"], ref["words"]) and np.array_equal(enc["offs"], ref["offs"])
+    m = rb.RansMatrix(enc, torch.from_numpy(step))
+    _check_y(m.gemv(torch.from_numpy(x).cuda()).cpu().numpy(), _y64(codes, step, x))
+    xb = torch.from_numpy(x).bfloat16()
+    _check_y(m.gemv_bf16(xb.cuda()).cpu().numpy(), _y64(codes, step, xb.float().numpy()))
+    dec = m.decode().float().cpu().numpy()
+    assert np.array_equal(dec, (torch.from_numpy(codes).float() * torch.from_numpy(step)).bfloat16().float().numpy())
+
+
 def test_unstaged_fallback_high_entropy(torch, rb):
     """Spans larger than the shared-memory stage (8 bits/symbol, R=16, C=1024)
     take the global-memory path; results must not change."""

@@ -99,6 +99,42 @@ def test_encoder_random_shapes_against_oracle(lib):
             assert np.array_equal(a[k], b[k]), (trial, k)
 
 
+@settings(max_examples=40, deadline=None)
+@given(data=st.data())
+def test_encoder_edge_distributions_against_oracle(lib, data):
+    """The C++ producer byte-for-byte against the oracle restatement of the
+    reference encoder on the distributions that stress the 12-bit frequency
+    normalisation: two symbols only, the alphabet's two extremes only, one
+    dominant symbol with many singletons (each must keep frequency >= 1), the
+    whole alphabet uniformly, and Laplacian codes of any scale."""
+    R = data.draw(st.sampled_from([1, 2, 4, 8, 16]))
+    C = 32 * data.draw(st.integers(1, 4))
+    rows, cols = R * data.draw(st.integers(1, 4)), C * data.draw(st.integers(1, 3))
+    kind = data.draw(st.sampled_from(["two", "extremes", "dominant", "uniform", "laplace"]))
+    rng = np.random.default_rng(data.draw(st.integers(0, 2**31 - 1)))
+    if kind == "two":
+        a, b = sorted(rng.choice(256, 2, replace=False) - 128)
+        codes = np.where(rng.random((rows, cols)) < rng.uniform(0.001, 0.999), a, b)
+    elif kind == "extremes":
+        codes = np.where(rng.random((rows, cols)) < 0.5, -128, 127)
+    elif kind == "dominant":
+        codes = np.zeros((rows, cols), np.int64)
+        k = min(rows * cols - 1, 200)
+        idx = rng.choice(rows * cols, k, replace=False)
+        codes.flat[idx] = rng.choice(np.r_[-128:0, 1:128], k)   # up to 200 rare symbols
+    elif kind == "uniform":
+        codes = rng.integers(-128, 128, (rows, cols))
+    else:
+        codes = np.clip(np.round(rng.laplace(0, rng.uniform(0.05, 40), (rows, cols))), -128, 127)
+    codes = codes.astype(np.int32)
+    if len(np.unique(codes)) < 2:                              # a single symbol cannot be coded
+        codes.flat[0] = codes.flat[0] + (1 if codes.flat[0] < 127 else -1)
+    a = rb.encode(codes, R, C, nthreads=3)
+    b = orc.encode(codes, R, C)
+    for k in ("words", "offs", "table"):
+        assert np.array_equal(a[k], b[k]), (kind, k)
+
+
 def test_encoder_errors(lib):
     with pytest.raises(AssertionError):
         rb.encode(np.zeros((8, 64), np.int32), 8, 64)          # single symbol
