@@ -10,7 +10,8 @@ dependent phases from one persistent grid, through the C ABI.
     output) read the finished output in every one of 20 back-to-back launches;
   * a dependency that never arrives (a second rank that does not exist, on
     one GPU) makes the bounded wait run out: the status comes back, the
-    context stays usable and the status clears once read.
+    context stays usable and the status clears once read;
+  * every tile height R, and random chains of odd shapes and phase groupings.
 """
 import numpy as np
 import pytest
@@ -169,3 +170,48 @@ def test_chain_every_tile_height(torch, rb, R):
     for k in range(2):
         _check_y(ys[k].cpu().numpy(), orc.gemv(codes_l[k], steps[k].astype(np.float64), xb))
     _check_y(ys[2].cpu().numpy(), orc.gemv(codes_l[2], np.ones(512), ys[1].cpu().numpy().astype(np.float64)))
+
+
+@pytest.mark.parametrize("seed", range(6))
+def test_random_chains(torch, rb, seed):
+    """Random chains through the kernel (the planner's side of the same cases
+    is checked without a GPU in tests/test_host.py): tile heights R 1-16, tile
+    widths 64-640 columns, 1-7 column tiles, 1-80 row blocks, 1.25-6 bits
+    per weight, random phase groupings, bf16 and prescaled fp32 activations
+    mixed; every output of two back-to-back launches against float64."""
+    rng = np.random.default_rng(900 + seed)
+    R = (1, 2, 4, 8, 16, 8)[seed]
+    n = int(rng.integers(3, 8))
+    raw = rng.integers(0, n, n)
+    used = sorted(set(raw.tolist()))
+    phases = [used.index(v) for v in raw.tolist()]
+    mats, codes_l, steps, xs, xref, pre = [], [], [], [], [], []
+    for i in range(n):
+        C = int(rng.choice([64, 256, 512, 640]))
+        rows, cols = R * int(rng.integers(1, 81)), C * int(rng.integers(1, 8))
+        bits = float(rng.choice([1.25, 2.25, 3.25, 4.25, 6.0]))
+        codes = orc.synth_codes(rows, cols, bits, str(rng.choice(["laplace", "gauss"])), seed=1000 * seed + i)
+        step = (0.01 * rng.uniform(0.5, 1.5, cols)).astype(np.float32)
+        x = rng.standard_normal(cols).astype(np.float32)
+        mats.append(rb.RansMatrix(rb.encode(codes, R, C), torch.from_numpy(step)))
+        codes_l.append(codes)
+        if rng.random() < 0.5:                                   # bf16 x, step applied in the kernel
+            xb = torch.from_numpy(x).bfloat16()
+            xs.append(xb.cuda())
+            xref.append(xb.float().numpy().astype(np.float64) * step.astype(np.float64))
+            pre.append(False)
+        else:                                                    # fp32 x already times the step
+            xp = (torch.from_numpy(x) * torch.from_numpy(step)).float()
+            xs.append(xp.cuda())
+            xref.append(xp.numpy().astype(np.float64))
+            pre.append(True)
+    ys = [torch.empty(m.rows, device="cuda") for m in mats]
+    ch = rb.RansChain(mats, xs, ys, phases, prescaled_x=pre)
+    for _ in range(2):
+        for y in ys:
+            y.fill_(float("nan"))
+        ch()
+    ch.check()
+    torch.cuda.synchronize()
+    for i in range(n):
+        _check_y(ys[i].cpu().numpy(), orc.gemv(codes_l[i], np.ones(codes_l[i].shape[1]), xref[i]))
