@@ -1958,9 +1958,10 @@ __global__ void __launch_bounds__(kThreads, RB_MINB) gemv_chain_kernel(const Cha
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const SmemMap sm = smem_map(warp);
     const uint32_t* cur = nullptr;    // table now in shared memory
-    // thread 0: a chunk taken ahead -- the queue's old value and the status,
-    // both read when this chunk starts and first used when it ends, so the
-    // round trip overlaps the chunk instead of delaying its start
+    // thread 0: the next chunk -- the queue's old value and the status.  For a
+    // chunk that may be taken ahead both are read when this chunk starts and
+    // first used when it ends, so the round trip overlaps the chunk (`ahead`);
+    // otherwise they are read when it ends.
     bool ahead = false;
     uint32_t ahead_raw = 0;
     int32_t ahead_status = 0;
